@@ -1,0 +1,244 @@
+/*
+ * rusttorch_cuda.h — C ABI of the B200 (sm_100a) implementation of
+ * rusttorch-core's data-parallel tensor hot path.
+ *
+ * The library (librusttorch_cuda.so) is the device-side counterpart of
+ * rusttorch-core's `ffi` feature (rusttorch-core/src/ffi/{mod,tensor,ops}.rs):
+ * the same descriptor and result conventions, one entry point per hot-path op,
+ * with tensors living in GPU memory instead of being copied in and out of
+ * Rust-owned host arrays.  A `Tensor` device-storage variant in rusttorch-core
+ * dispatches its ops here; the ops API and the PyO3 bindings do not change.
+ *
+ * Conventions
+ *  - Every fallible call returns rtc_result by value.  On failure `error_msg`
+ *    is a NUL-terminated message owned by the caller until passed to
+ *    rtc_free_error_message(), formatted like rusttorch's TensorError Display
+ *    (rusttorch-core/src/error.rs:69-160), and `code` names the variant.
+ *  - Inputs are validated on the host before anything is launched, in the
+ *    reference's order (dtype before shape for binary ops, shapes before
+ *    hyperparameters for the optimizers).  The library never aborts.
+ *  - Tensors are C-contiguous (`strides` NULL or row-major).  `data` is a
+ *    device pointer on `device`; outputs are preallocated by the caller and
+ *    may alias inputs of the same shape (in-place use).
+ *  - Kernels run on the calling thread's stream (rtc_set_stream; default: the
+ *    per-thread default stream) and calls return once the work is queued,
+ *    except the scalar reductions (rtc_sum/mean/max/min, rtc_sharded_*),
+ *    which return their value and so wait for it.
+ *  - dtype: every op implements float32 (RTC_F32).  Other dtypes return
+ *    RTC_UNSUPPORTED after the reference's own dtype checks have run.
+ */
+#ifndef RUSTTORCH_CUDA_H
+#define RUSTTORCH_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RTC_VERSION_STRING "0.1.0"
+
+/* dtype codes of CTensorDescriptor.dtype (rusttorch-core/src/ffi/tensor.rs:25) */
+enum { RTC_F32 = 0, RTC_F64 = 1, RTC_I32 = 2, RTC_I64 = 3 };
+
+/* rtc_result.code: the TensorError variant (rusttorch-core/src/error.rs:10-67) */
+typedef enum {
+  RTC_OK = 0,
+  RTC_SHAPE_MISMATCH = 1,    /* TensorError::ShapeMismatch     error.rs:12-16 */
+  RTC_DTYPE_MISMATCH = 2,    /* TensorError::DTypeMismatch     error.rs:19-23 */
+  RTC_EMPTY_TENSOR = 3,      /* TensorError::EmptyTensor       error.rs:26 */
+  RTC_INVALID_DIMENSION = 4, /* TensorError::InvalidDimension  error.rs:29-33 */
+  RTC_INVALID_ARGUMENT = 5,  /* TensorError::InvalidArgument   error.rs:46 */
+  RTC_SIZE_OVERFLOW = 6,     /* TensorError::SizeOverflow      error.rs:43 */
+  RTC_UNSUPPORTED = 7,       /* dtype/layout this library does not implement */
+  RTC_BACKEND_ERROR = 8      /* CUDA or NCCL failure (TensorError::Other, error.rs:66) */
+} rtc_status;
+
+/* CTensorDescriptor (rusttorch-core/src/ffi/tensor.rs:13-26) plus the device
+ * that holds `data`. */
+typedef struct {
+  void* data;            /* device pointer (or NULL when numel == 0) */
+  const size_t* shape;   /* ndim extents */
+  const size_t* strides; /* element strides; NULL means C-contiguous */
+  size_t ndim;
+  size_t numel;          /* must equal the product of shape */
+  int dtype;             /* RTC_F32 ... RTC_I64 */
+  int device;            /* CUDA device ordinal */
+} rtc_tensor;
+
+/* CResult (rusttorch-core/src/ffi/tensor.rs:38-64) plus the variant code.
+ * The first two members have CResult's layout. */
+typedef struct {
+  bool success;
+  char* error_msg; /* NULL on success */
+  int code;        /* rtc_status */
+} rtc_result;
+
+/* ---------------------------------------------------------------- lifecycle */
+/* rusttorch_version, ffi/mod.rs:45-48.  Static string, do not free. */
+const char* rtc_version(void);
+/* rusttorch_init, ffi/mod.rs:25-32: initialises the CUDA context of every
+ * visible device.  Optional; every entry point initialises lazily. */
+rtc_result rtc_init(void);
+/* rusttorch_cleanup, ffi/mod.rs:38-41: releases library-held device state. */
+void rtc_cleanup(void);
+/* rusttorch_free_error_message, ffi/tensor.rs:68-73 */
+void rtc_free_error_message(char* msg);
+
+/* Stream (a cudaStream_t) for the calling thread's subsequent calls; NULL
+ * selects the per-thread default stream. */
+rtc_result rtc_set_stream(void* stream);
+void* rtc_get_stream(void);
+/* Waits for the calling thread's stream. */
+rtc_result rtc_synchronize(void);
+int rtc_device_count(void);
+
+/* Memory helpers for callers without the CUDA runtime (no reference
+ * counterpart: the reference owns host memory through ndarray). */
+rtc_result rtc_malloc(int device, size_t bytes, void** out);
+rtc_result rtc_free(int device, void* ptr);
+rtc_result rtc_memcpy_h2d(int device, void* dst, const void* src, size_t bytes);
+rtc_result rtc_memcpy_d2h(int device, void* dst, const void* src, size_t bytes);
+rtc_result rtc_host_alloc(size_t bytes, void** out); /* page-locked host memory */
+rtc_result rtc_host_free(void* ptr);
+
+/* Seeded synthetic data on the device: element i depends only on
+ * (seed, offset + i).  uniform in [lo, hi); normal(mean, std). */
+rtc_result rtc_fill_uniform(const rtc_tensor* out, uint64_t seed, uint64_t offset, float lo,
+                            float hi);
+rtc_result rtc_fill_normal(const rtc_tensor* out, uint64_t seed, uint64_t offset, float mean,
+                           float std);
+
+/* -------------------------------------------------- elementwise (f32, bit-exact) */
+/* rusttorch_add, ffi/ops.rs:21-40 -> ops::add, ops/elementwise.rs:14-94 */
+rtc_result rtc_add(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+/* rusttorch_mul, ffi/ops.rs:44-63 -> ops::mul, ops/elementwise.rs:97-127 */
+rtc_result rtc_mul(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+/* rusttorch_sub, ffi/ops.rs:67-86 -> ops::sub, ops/elementwise.rs:130-160 */
+rtc_result rtc_sub(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+/* rusttorch_div, ffi/ops.rs:90-109 -> ops::div, ops/elementwise.rs:163-197 */
+rtc_result rtc_div(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+/* ops::add_scalar, ops/elementwise.rs:200-210 (no reference FFI export) */
+rtc_result rtc_add_scalar(const rtc_tensor* x, float scalar, const rtc_tensor* out);
+/* ops::mul_scalar, ops/elementwise.rs:213-223 (no reference FFI export) */
+rtc_result rtc_mul_scalar(const rtc_tensor* x, float scalar, const rtc_tensor* out);
+/* ops::mul_scalar(&ops::add(a, b)?, s) in one pass (elementwise.rs:14 then :213) */
+rtc_result rtc_add_mul_scalar(const rtc_tensor* a, const rtc_tensor* b, float scalar,
+                              const rtc_tensor* out);
+/* ops::fused_multiply_add, ops/simd.rs:275-370: a*b + c, two roundings */
+rtc_result rtc_fused_multiply_add(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* c,
+                                  const rtc_tensor* out);
+/* ops::add_simd / mul_simd / relu_simd / mul_scalar_simd (ops/simd.rs:14, :95,
+ * :176, :225): same values as the plain ops, their own error contexts. */
+rtc_result rtc_add_simd(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+rtc_result rtc_mul_simd(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+rtc_result rtc_relu_simd(const rtc_tensor* x, const rtc_tensor* out);
+rtc_result rtc_mul_scalar_simd(const rtc_tensor* x, float scalar, const rtc_tensor* out);
+
+/* ------------------------------------------------------------- activations */
+/* rusttorch_relu, ffi/ops.rs:117-132 -> ops::relu, ops/activation.rs:8-18 */
+rtc_result rtc_relu(const rtc_tensor* x, const rtc_tensor* out);
+/* rusttorch_leaky_relu, ffi/ops.rs:199-215 -> ops::leaky_relu, activation.rs:170-191 */
+rtc_result rtc_leaky_relu(const rtc_tensor* x, const rtc_tensor* out, float alpha);
+/* rusttorch_sigmoid, ffi/ops.rs:136-153 -> ops::sigmoid, activation.rs:21-37 */
+rtc_result rtc_sigmoid(const rtc_tensor* x, const rtc_tensor* out);
+/* rusttorch_tanh, ffi/ops.rs:157-174 -> ops::tanh, activation.rs:40-56 */
+rtc_result rtc_tanh(const rtc_tensor* x, const rtc_tensor* out);
+/* rusttorch_gelu, ffi/ops.rs:178-195 -> ops::gelu, activation.rs:61-88 */
+rtc_result rtc_gelu(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::swish (SiLU), activation.rs:263-279 */
+rtc_result rtc_swish(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::elu, activation.rs:195-222 (alpha <= 0 -> RTC_INVALID_ARGUMENT) */
+rtc_result rtc_elu(const rtc_tensor* x, const rtc_tensor* out, float alpha);
+/* ops::selu, activation.rs:228-259 */
+rtc_result rtc_selu(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::mish, activation.rs:284-314 */
+rtc_result rtc_mish(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::softplus, activation.rs:319-346 */
+rtc_result rtc_softplus(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::softsign, activation.rs:351-367 */
+rtc_result rtc_softsign(const rtc_tensor* x, const rtc_tensor* out);
+/* ops::softmax(t, dim), activation.rs:92-167 */
+rtc_result rtc_softmax(const rtc_tensor* x, size_t dim, const rtc_tensor* out);
+
+/* -------------------------------------------------------------- reductions */
+/* rusttorch_sum, ffi/ops.rs:223-238 -> ops::sum, ops/reduction.rs:7-14 */
+rtc_result rtc_sum(const rtc_tensor* x, double* out_value);
+/* rusttorch_mean, ffi/ops.rs:241-256 -> ops::mean, reduction.rs:17-26 */
+rtc_result rtc_mean(const rtc_tensor* x, double* out_value);
+/* rusttorch_max, ffi/ops.rs:259-274 -> ops::max, reduction.rs:29-49 */
+rtc_result rtc_max(const rtc_tensor* x, double* out_value);
+/* rusttorch_min, ffi/ops.rs:277-292 -> ops::min, reduction.rs:52-72 */
+rtc_result rtc_min(const rtc_tensor* x, double* out_value);
+/* sum, mean, max and min from one pass over x (no reference counterpart; each
+ * value equals the corresponding single op).  out[4] = {sum, mean, max, min}. */
+rtc_result rtc_stats(const rtc_tensor* x, double out[4]);
+/* ops::sum_dim, reduction.rs:75-108: out has shape without `dim`. */
+rtc_result rtc_sum_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out);
+/* ops::mean_dim, reduction.rs:111-150 */
+rtc_result rtc_mean_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out);
+/* max along `dim` (no reference counterpart: the reference's global max fold,
+ * reduction.rs:29-49, applied to every lane). */
+rtc_result rtc_max_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out);
+
+/* ------------------------------------------------------- optimizer updates */
+/* ops::adam_update, ops/optimizer.rs:207-354.  Writes p', m', v' into the
+ * *_out tensors (which may be p, m, v themselves). */
+rtc_result rtc_adam_update(const rtc_tensor* params, const rtc_tensor* grads, const rtc_tensor* m,
+                           const rtc_tensor* v, double learning_rate, double beta1, double beta2,
+                           double epsilon, uint64_t timestep, const rtc_tensor* params_out,
+                           const rtc_tensor* m_out, const rtc_tensor* v_out);
+/* ops::adamw_update, ops/optimizer.rs:379-440 */
+rtc_result rtc_adamw_update(const rtc_tensor* params, const rtc_tensor* grads,
+                            const rtc_tensor* m, const rtc_tensor* v, double learning_rate,
+                            double beta1, double beta2, double epsilon, double weight_decay,
+                            uint64_t timestep, const rtc_tensor* params_out,
+                            const rtc_tensor* m_out, const rtc_tensor* v_out);
+/* ops::sgd_update, ops/optimizer.rs:42-86 */
+rtc_result rtc_sgd_update(const rtc_tensor* params, const rtc_tensor* grads,
+                          double learning_rate, const rtc_tensor* params_out);
+/* ops::sgd_momentum_update, ops/optimizer.rs:108-177 */
+rtc_result rtc_sgd_momentum_update(const rtc_tensor* params, const rtc_tensor* grads,
+                                   const rtc_tensor* velocity, double learning_rate,
+                                   double momentum, const rtc_tensor* params_out,
+                                   const rtc_tensor* velocity_out);
+
+/* --------------------------------------------- sharded global reductions */
+/* A tensor split into contiguous shards, one per GPU or process, reduces to
+ * the reference's sum/mean/max/min of the whole (reduction.rs:7-72) in two
+ * steps: every shard is summarised on its own GPU, the summaries (a few bytes
+ * each) are exchanged by any collective (NCCL all-gather in bench.py), and
+ * rtc_shard_combine folds them in shard order.  The summary keeps what the
+ * reference's order-dependent max/min folds need across shard boundaries. */
+typedef struct {
+  double sum;          /* f64 sum of the shard */
+  uint64_t count;      /* elements in the shard */
+  float max;           /* the shard's max fold (see max_kind) */
+  float min_nonnan;    /* min fold over the shard's non-NaN elements (+inf if none) */
+  int32_t max_kind;    /* 0: empty shard; 1: max fold of the shard alone;
+                          2: the shard holds a NaN, so the fold's value after
+                             it is `max` whatever came before */
+  int32_t first_nan;   /* the shard's first element is NaN */
+} rtc_shard_summary;
+
+/* Summarise one shard (device tensor).  Waits for the result. */
+rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard_summary* out);
+/* Fold n summaries in shard order (host only, no GPU needed).
+ * out[4] = {sum, mean, max, min} of the concatenated tensor; an empty total
+ * writes out[0] = 0 and returns RTC_EMPTY_TENSOR. */
+rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]);
+
+/* ------------------------------------- flat float32 API (device pointers) */
+/* rusttorch_relu_f32 / add_f32 / mul_f32, ffi/ops.rs:348-389: contiguous f32
+ * buffers of `size` elements on the current device. */
+rtc_result rtc_relu_f32(const float* input, float* output, size_t size);
+rtc_result rtc_add_f32(const float* a, const float* b, float* output, size_t size);
+rtc_result rtc_mul_f32(const float* a, const float* b, float* output, size_t size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RUSTTORCH_CUDA_H */

@@ -1,0 +1,111 @@
+/*
+ * rt_oracle.h — CPU restatement of rusttorch-core's data-parallel hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA
+ * path in rusttorch_b200/.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference leg of bench.py may load it.  The product never
+ * links, calls or falls back to it.
+ *
+ * Every function restates one reference function, in the reference's f32
+ * operation order, and cites the file:line it follows (paths relative to the
+ * rusttorch repository root; "core/" = rusttorch-core/).  Compile with
+ * -ffp-contract=off -fno-fast-math so that each f32 operation rounds once, as
+ * Rust (which never contracts a*b+c) does.  Transcendentals call glibc libm
+ * (expf/tanhf/logf), which is what Rust's f32::exp/tanh/ln lower to on
+ * x86_64-linux-gnu.
+ *
+ * Third-party arithmetic the reference delegates to, restated here:
+ *  - ndarray 0.15 (rusttorch Cargo.toml:15; no Cargo.lock, so 0.15.x is not
+ *    pinned further): ArrayBase::sum_axis / mean_axis (order of the dim sums
+ *    and of softmax's row sum) and numeric_util::unrolled_fold (eight-way
+ *    unrolled lane sum).  No reference test checks these values, so this part
+ *    of the oracle is pinned only by the restatement itself.
+ *  - Rust core: Iterator::max_by/min_by via cmp::max_by/min_by (ties and NaN
+ *    ordering of max/min), f32::max (relu), f64::powf (glibc pow).
+ *
+ * Error codes mirror core/src/error.rs:10-67 (see RTO_* below) and are the
+ * same numbers the CUDA C-ABI returns.
+ */
+#ifndef RT_ORACLE_H
+#define RT_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  RTO_OK = 0,
+  RTO_SHAPE_MISMATCH = 1,
+  RTO_DTYPE_MISMATCH = 2,
+  RTO_EMPTY_TENSOR = 3,
+  RTO_INVALID_DIMENSION = 4,
+  RTO_INVALID_ARGUMENT = 5,
+};
+
+/* ---- elementwise: core/src/ops/elementwise.rs, core/src/ops/simd.rs ---- */
+void rto_add(const float* a, const float* b, float* out, size_t n);
+void rto_sub(const float* a, const float* b, float* out, size_t n);
+void rto_mul(const float* a, const float* b, float* out, size_t n);
+void rto_div(const float* a, const float* b, float* out, size_t n);
+void rto_add_scalar(const float* x, float s, float* out, size_t n);
+void rto_mul_scalar(const float* x, float s, float* out, size_t n);
+void rto_fused_multiply_add(const float* a, const float* b, const float* c, float* out, size_t n);
+
+/* ---- activations: core/src/ops/activation.rs ---- */
+void rto_relu(const float* x, float* out, size_t n);
+void rto_leaky_relu(const float* x, float alpha, float* out, size_t n);
+void rto_sigmoid(const float* x, float* out, size_t n);
+void rto_tanh(const float* x, float* out, size_t n);
+void rto_gelu(const float* x, float* out, size_t n);
+void rto_swish(const float* x, float* out, size_t n);
+int  rto_elu(const float* x, float alpha, float* out, size_t n);
+void rto_selu(const float* x, float* out, size_t n);
+void rto_mish(const float* x, float* out, size_t n);
+void rto_softplus(const float* x, float* out, size_t n);
+void rto_softsign(const float* x, float* out, size_t n);
+/* softmax along `dim` of a C-contiguous tensor. */
+int  rto_softmax(const float* x, const size_t* shape, size_t ndim, size_t dim, float* out);
+
+/* ---- reductions: core/src/ops/reduction.rs ---- */
+double rto_sum(const float* x, size_t n);
+int    rto_mean(const float* x, size_t n, double* out);
+int    rto_max(const float* x, size_t n, double* out);
+int    rto_min(const float* x, size_t n, double* out);
+int    rto_sum_dim(const float* x, const size_t* shape, size_t ndim, size_t dim, float* out);
+int    rto_mean_dim(const float* x, const size_t* shape, size_t ndim, size_t dim, float* out);
+/* max along a dim: no reference counterpart (the reference has no max_dim);
+ * defined as the reference's global-max fold applied to each lane. */
+int    rto_max_dim(const float* x, const size_t* shape, size_t ndim, size_t dim, float* out);
+
+/* ---- optimizer rules: core/src/ops/optimizer.rs ---- */
+int rto_adam_update(const float* p, const float* g, const float* m, const float* v, size_t n,
+                    double lr, double beta1, double beta2, double eps, uint64_t t,
+                    float* p_out, float* m_out, float* v_out);
+int rto_adamw_update(const float* p, const float* g, const float* m, const float* v, size_t n,
+                     double lr, double beta1, double beta2, double eps, double weight_decay,
+                     uint64_t t, float* p_out, float* m_out, float* v_out);
+int rto_sgd_update(const float* p, const float* g, size_t n, double lr, float* p_out);
+int rto_sgd_momentum_update(const float* p, const float* g, const float* vel, size_t n,
+                            double lr, double momentum, float* p_out, float* vel_out);
+
+/* ---- seeded synthetic inputs (the generator the tests and the CPU baseline
+ * use; the CUDA library carries an identical device generator).  Element i of
+ * a stream depends only on (seed, i), so any slice can be regenerated alone.
+ *   uniform: u = (splitmix64(seed, i) >> 40) * 2^-24 in [0,1); lo + (hi-lo)*u
+ *   normal : Box-Muller in f64 on two 26-bit uniforms from one 64-bit draw  */
+void rto_fill_uniform(float* out, size_t n, uint64_t seed, uint64_t offset, float lo, float hi);
+void rto_fill_normal(float* out, size_t n, uint64_t seed, uint64_t offset, float mean, float std);
+
+/* Threads used by the reference's rayon-parallel ops (add when n >= 10000);
+ * defaults to the number of online CPUs, like rayon's global pool
+ * (core/src/ffi/mod.rs:25-32).  0 restores the default. */
+void rto_set_threads(int n);
+int  rto_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

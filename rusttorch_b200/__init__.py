@@ -1,0 +1,265 @@
+"""rusttorch_b200 — rusttorch-core's data-parallel tensor hot path on B200.
+
+The Python surface mirrors rusttorch's PyO3 module (rusttorch-py/src/lib.rs):
+the same function names, argument meaning and error behaviour (every failure
+raises ValueError, here the RusttorchError subclass carrying the TensorError
+variant).  The difference is where the data lives: a `Tensor` here is a
+float32 buffer in GPU memory, and every op is one call into
+librusttorch_cuda.so (see include/rusttorch_cuda.h).  Ops are asynchronous on
+the calling thread's stream; `to_numpy()` and the scalar reductions wait.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_double, c_void_p
+
+import numpy as np
+
+from . import _native
+from ._native import F32, RusttorchError, check, lib
+
+__all__ = [
+    "Tensor", "RusttorchError", "version",
+    "add", "sub", "mul", "div", "add_scalar", "mul_scalar", "add_mul_scalar",
+    "fused_multiply_add", "add_simd", "mul_simd", "relu_simd", "mul_scalar_simd",
+    "relu", "leaky_relu", "sigmoid", "tanh", "gelu", "swish", "elu", "selu", "mish",
+    "softplus", "softsign", "softmax",
+    "sum", "mean", "max", "min", "stats", "sum_dim", "mean_dim", "max_dim",
+    "adam_update", "adamw_update", "sgd_update", "sgd_momentum_update",
+    "synchronize",
+]
+
+
+def version() -> str:
+    return lib().rtc_version().decode()
+
+
+def synchronize() -> None:
+    check(lib().rtc_synchronize())
+
+
+class Tensor:
+    """A C-contiguous float32 tensor in the memory of one GPU."""
+
+    def __init__(self, shape, device: int = 0, *, ptr: int | None = None, owner=None):
+        self._shape = tuple(int(d) for d in shape)
+        self.device = int(device)
+        self._owned = ptr is None
+        self._owner = owner          # keeps a borrowed buffer alive
+        if ptr is None:
+            out = c_void_p()
+            check(lib().rtc_malloc(self.device, self.nbytes, ctypes.byref(out)))
+            ptr = out.value or 0
+        self.ptr = int(ptr)
+        self._desc = _native.Desc(self.ptr, self._shape, F32, self.device)
+
+    # ---- construction (rusttorch-py/src/lib.rs:35-61) ---------------------
+    @staticmethod
+    def zeros(shape, device: int = 0) -> "Tensor":
+        return Tensor.from_numpy(np.zeros(list(shape), dtype=np.float32), device)
+
+    @staticmethod
+    def ones(shape, device: int = 0) -> "Tensor":
+        return Tensor.from_numpy(np.ones(list(shape), dtype=np.float32), device)
+
+    @staticmethod
+    def empty(shape, device: int = 0) -> "Tensor":
+        return Tensor(shape, device)
+
+    @staticmethod
+    def from_numpy(array, device: int = 0) -> "Tensor":
+        a = np.asarray(array)
+        if a.dtype != np.float32:
+            raise RusttorchError("only float32 arrays are supported", _native.UNSUPPORTED)
+        if not a.flags.c_contiguous:
+            raise ValueError("Array must be contiguous")
+        t = Tensor(a.shape, device)
+        if t.nbytes:
+            check(lib().rtc_memcpy_h2d(t.device, c_void_p(t.ptr), a.ctypes.data_as(c_void_p),
+                                       t.nbytes))
+        return t
+
+    @staticmethod
+    def from_device_ptr(ptr: int, shape, device: int = 0, owner=None) -> "Tensor":
+        """Borrow an existing device buffer (e.g. a torch tensor's data_ptr())."""
+        return Tensor(shape, device, ptr=ptr, owner=owner)
+
+    # ---- metadata (rusttorch-py/src/lib.rs:63-79) -------------------------
+    def shape(self) -> list[int]:
+        return list(self._shape)
+
+    def ndim(self) -> int:
+        return len(self._shape)
+
+    def numel(self) -> int:
+        n = 1
+        for d in self._shape:
+            n *= d
+        return n
+
+    @property
+    def nbytes(self) -> int:
+        return self.numel() * 4
+
+    def __repr__(self) -> str:
+        return f"Tensor(shape={list(self._shape)}, dtype=float32)"
+
+    def to_numpy(self) -> np.ndarray:
+        out = np.empty(self._shape, dtype=np.float32)
+        if self.nbytes:
+            check(lib().rtc_memcpy_d2h(self.device, out.ctypes.data_as(c_void_p),
+                                       c_void_p(self.ptr), self.nbytes))
+        return out
+
+    @property
+    def desc(self):
+        return self._desc.ref
+
+    def __del__(self):
+        try:
+            if self._owned and self.ptr:
+                lib().rtc_free(self.device, c_void_p(self.ptr))
+                self.ptr = 0
+        except Exception:
+            pass
+
+
+def _like(x: Tensor, shape=None) -> Tensor:
+    return Tensor(x.shape() if shape is None else shape, x.device)
+
+
+def _binary(fn, a: Tensor, b: Tensor) -> Tensor:
+    out = _like(a)
+    check(fn(a.desc, b.desc, out.desc))
+    return out
+
+
+def _unary(fn, x: Tensor, *extra) -> Tensor:
+    out = _like(x)
+    check(fn(x.desc, out.desc, *extra))
+    return out
+
+
+# ---- elementwise (rusttorch-py/src/lib.rs:83-123, :400-435) ----------------
+def add(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_add, a, b)
+def mul(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_mul, a, b)
+def sub(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_sub, a, b)
+def div(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_div, a, b)
+def add_simd(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_add_simd, a, b)
+def mul_simd(a: Tensor, b: Tensor) -> Tensor: return _binary(lib().rtc_mul_simd, a, b)
+
+
+def add_scalar(t: Tensor, scalar: float) -> Tensor:
+    out = _like(t)
+    check(lib().rtc_add_scalar(t.desc, float(scalar), out.desc))
+    return out
+
+
+def mul_scalar(t: Tensor, scalar: float) -> Tensor:
+    out = _like(t)
+    check(lib().rtc_mul_scalar(t.desc, float(scalar), out.desc))
+    return out
+
+
+def mul_scalar_simd(t: Tensor, scalar: float) -> Tensor:
+    out = _like(t)
+    check(lib().rtc_mul_scalar_simd(t.desc, float(scalar), out.desc))
+    return out
+
+
+def add_mul_scalar(a: Tensor, b: Tensor, scalar: float) -> Tensor:
+    """mul_scalar(add(a, b), scalar) in one pass over memory."""
+    out = _like(a)
+    check(lib().rtc_add_mul_scalar(a.desc, b.desc, float(scalar), out.desc))
+    return out
+
+
+def fused_multiply_add(a: Tensor, b: Tensor, c: Tensor) -> Tensor:
+    out = _like(a)
+    check(lib().rtc_fused_multiply_add(a.desc, b.desc, c.desc, out.desc))
+    return out
+
+
+# ---- activations (rusttorch-py/src/lib.rs:126-208) --------------------------
+def relu(t: Tensor) -> Tensor: return _unary(lib().rtc_relu, t)
+def relu_simd(t: Tensor) -> Tensor: return _unary(lib().rtc_relu_simd, t)
+def sigmoid(t: Tensor) -> Tensor: return _unary(lib().rtc_sigmoid, t)
+def tanh(t: Tensor) -> Tensor: return _unary(lib().rtc_tanh, t)
+def gelu(t: Tensor) -> Tensor: return _unary(lib().rtc_gelu, t)
+def swish(t: Tensor) -> Tensor: return _unary(lib().rtc_swish, t)
+def selu(t: Tensor) -> Tensor: return _unary(lib().rtc_selu, t)
+def mish(t: Tensor) -> Tensor: return _unary(lib().rtc_mish, t)
+def softplus(t: Tensor) -> Tensor: return _unary(lib().rtc_softplus, t)
+def softsign(t: Tensor) -> Tensor: return _unary(lib().rtc_softsign, t)
+def leaky_relu(t: Tensor, alpha: float) -> Tensor: return _unary(lib().rtc_leaky_relu, t, float(alpha))
+def elu(t: Tensor, alpha: float) -> Tensor: return _unary(lib().rtc_elu, t, float(alpha))
+
+
+def softmax(t: Tensor, dim: int) -> Tensor:
+    out = _like(t)
+    check(lib().rtc_softmax(t.desc, int(dim), out.desc))
+    return out
+
+
+# ---- reductions (rusttorch-py/src/lib.rs:234-242; core reduction.rs) -------
+def _scalar(fn, t: Tensor) -> float:
+    v = c_double()
+    check(fn(t.desc, ctypes.byref(v)))
+    return v.value
+
+
+def sum(t: Tensor) -> float: return _scalar(lib().rtc_sum, t)     # noqa: A001
+def mean(t: Tensor) -> float: return _scalar(lib().rtc_mean, t)
+def max(t: Tensor) -> float: return _scalar(lib().rtc_max, t)     # noqa: A001
+def min(t: Tensor) -> float: return _scalar(lib().rtc_min, t)     # noqa: A001
+
+
+def stats(t: Tensor) -> tuple[float, float, float, float]:
+    """(sum, mean, max, min) from one pass."""
+    v = (c_double * 4)()
+    check(lib().rtc_stats(t.desc, v))
+    return tuple(v)
+
+
+def _dim(fn, t: Tensor, dim: int) -> Tensor:
+    dim = int(dim)
+    shape = [d for i, d in enumerate(t.shape()) if i != dim] if 0 <= dim < t.ndim() else []
+    out = _like(t, shape)
+    check(fn(t.desc, dim, out.desc))
+    return out
+
+
+def sum_dim(t: Tensor, dim: int) -> Tensor: return _dim(lib().rtc_sum_dim, t, dim)
+def mean_dim(t: Tensor, dim: int) -> Tensor: return _dim(lib().rtc_mean_dim, t, dim)
+def max_dim(t: Tensor, dim: int) -> Tensor: return _dim(lib().rtc_max_dim, t, dim)
+
+
+# ---- optimizers (rusttorch-py/src/lib.rs:278-369) --------------------------
+def adam_update(params, gradients, m, v, learning_rate, beta1, beta2, epsilon, timestep):
+    po, mo, vo = _like(params), _like(params), _like(params)
+    check(lib().rtc_adam_update(params.desc, gradients.desc, m.desc, v.desc, float(learning_rate),
+                                float(beta1), float(beta2), float(epsilon), int(timestep),
+                                po.desc, mo.desc, vo.desc))
+    return po, mo, vo
+
+
+def adamw_update(params, gradients, m, v, learning_rate, beta1, beta2, epsilon, weight_decay,
+                 timestep):
+    po, mo, vo = _like(params), _like(params), _like(params)
+    check(lib().rtc_adamw_update(params.desc, gradients.desc, m.desc, v.desc,
+                                 float(learning_rate), float(beta1), float(beta2), float(epsilon),
+                                 float(weight_decay), int(timestep), po.desc, mo.desc, vo.desc))
+    return po, mo, vo
+
+
+def sgd_update(params, gradients, learning_rate):
+    po = _like(params)
+    check(lib().rtc_sgd_update(params.desc, gradients.desc, float(learning_rate), po.desc))
+    return po
+
+
+def sgd_momentum_update(params, gradients, velocity, learning_rate, momentum):
+    po, vo = _like(params), _like(params)
+    check(lib().rtc_sgd_momentum_update(params.desc, gradients.desc, velocity.desc,
+                                        float(learning_rate), float(momentum), po.desc, vo.desc))
+    return po, vo

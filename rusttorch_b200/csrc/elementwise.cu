@@ -1,0 +1,326 @@
+// elementwise.cu — streaming kernels for the elementwise, scalar, activation
+// and optimizer-update ops of rusttorch-core (ops/elementwise.rs, simd.rs,
+// activation.rs, optimizer.rs).
+//
+// All of these are HBM-bound: per element they move 8 B (unary), 12 B
+// (binary), 16 B (fma) or 28 B (Adam/AdamW) and do a few to a few dozen flops.
+// Each thread moves 16-byte vectors (LDG.128 / STG.128) with U independent
+// vectors per stream in flight, so an SM with 2048 resident threads keeps
+// 2048 * U * 16 B * streams in flight — far above the ~40 KB per SM that
+// Little's law asks for at HBM3e latency.  Loads and stores use the streaming
+// cache hint (.cs): every byte is touched once.  Pointers that are not all
+// 16-byte aligned take a scalar grid-stride kernel instead (same results).
+#include "rt_internal.h"
+#include "rt_ops.cuh"
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+namespace rt {
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0) device = 0;
+  if ((size_t)device >= cache.size()) cache.resize(device + 1, 0);
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0)
+      v = 148;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+namespace {
+
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ void st4(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+
+template <class F>
+__device__ __forceinline__ float4 map4(const F& f, float4 a) {
+  return make_float4(f(a.x), f(a.y), f(a.z), f(a.w));
+}
+template <class F>
+__device__ __forceinline__ float4 map4(const F& f, float4 a, float4 b) {
+  return make_float4(f(a.x, b.x), f(a.y, b.y), f(a.z, b.z), f(a.w, b.w));
+}
+template <class F>
+__device__ __forceinline__ float4 map4(const F& f, float4 a, float4 b, float4 c) {
+  return make_float4(f(a.x, b.x, c.x), f(a.y, b.y, c.y), f(a.z, b.z, c.z), f(a.w, b.w, c.w));
+}
+
+template <int NIN>
+struct In {
+  const float* p[NIN];
+};
+
+template <class F, int NIN>
+__device__ __forceinline__ float apply1(const F& f, const In<NIN>& in, size_t i) {
+  if constexpr (NIN == 1) return f(in.p[0][i]);
+  else if constexpr (NIN == 2) return f(in.p[0][i], in.p[1][i]);
+  else return f(in.p[0][i], in.p[1][i], in.p[2][i]);
+}
+
+// Vectorised map: out[i] = f(in0[i], ...).  The block's tile is U vectors per
+// thread, strided by blockDim so each load instruction is fully coalesced.
+template <class F, int NIN, int U>
+__global__ void __launch_bounds__(kThreads) map_vec_kernel(In<NIN> in, float* out, size_t n, F f) {
+  const size_t n4 = n >> 2;
+  const size_t tile = (size_t)kThreads * U;
+  for (size_t base = (size_t)blockIdx.x * tile + threadIdx.x; base < n4;
+       base += (size_t)gridDim.x * tile) {
+    float4 v[NIN][U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      if (j < n4) {
+#pragma unroll
+        for (int k = 0; k < NIN; k++) v[k][u] = ld4(in.p[k] + 4 * j);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      if (j < n4) {
+        float4 r;
+        if constexpr (NIN == 1) r = map4(f, v[0][u]);
+        else if constexpr (NIN == 2) r = map4(f, v[0][u], v[1][u]);
+        else r = map4(f, v[0][u], v[1][u], v[2][u]);
+        st4(out + 4 * j, r);
+      }
+    }
+  }
+  // n % 4 tail elements
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const size_t i = (n4 << 2) + threadIdx.x;
+    out[i] = apply1<F, NIN>(f, in, i);
+  }
+}
+
+template <class F, int NIN>
+__global__ void __launch_bounds__(kThreads) map_scalar_kernel(In<NIN> in, float* out, size_t n, F f) {
+  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads)
+    out[i] = apply1<F, NIN>(f, in, i);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+// Grid for a streaming kernel: enough tiles to cover n, capped at a few
+// resident waves (the kernel grid-strides beyond that).
+unsigned grid_for(size_t units, size_t per_block) {
+  const size_t want = (units + per_block - 1) / per_block;
+  const size_t cap = (size_t)sm_count(current_device()) * 8 * 4;
+  return (unsigned)std::max<size_t>(1, std::min(want, cap));
+}
+
+template <class F, int NIN>
+cudaError_t launch_map(const F& f, const In<NIN>& in, float* out, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  bool vec = aligned16(out);
+  for (int k = 0; k < NIN; k++) vec = vec && aligned16(in.p[k]);
+  if (vec) {
+    constexpr int U = NIN == 1 ? 4 : (NIN == 2 ? 4 : 2);
+    const unsigned grid = grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * U);
+    map_vec_kernel<F, NIN, U><<<grid, kThreads, 0, s>>>(in, out, n, f);
+  } else {
+    const unsigned grid = grid_for(n, kThreads);
+    map_scalar_kernel<F, NIN><<<grid, kThreads, 0, s>>>(in, out, n, f);
+  }
+  return cudaGetLastError();
+}
+
+// sqrt_2_over_pi = (2.0_f32 / PI).sqrt() (activation.rs:73): f32 division and
+// square root, each correctly rounded.
+float gelu_k() {
+  volatile float two = 2.0f, pi = 3.14159265358979323846f;
+  return sqrtf(two / pi);
+}
+
+}  // namespace
+
+cudaError_t launch_unary(UnaryOp op, float param, const float* x, float* out, size_t n,
+                         cudaStream_t s) {
+  In<1> in{{x}};
+  switch (op) {
+    case kRelu: return launch_map(OpRelu{}, in, out, n, s);
+    case kLeakyRelu: return launch_map(OpLeakyRelu{param}, in, out, n, s);
+    case kSigmoid: return launch_map(OpSigmoid{}, in, out, n, s);
+    case kTanh: return launch_map(OpTanh{}, in, out, n, s);
+    case kGelu: return launch_map(OpGelu{gelu_k()}, in, out, n, s);
+    case kSwish: return launch_map(OpSwish{}, in, out, n, s);
+    case kElu: return launch_map(OpElu{param}, in, out, n, s);
+    case kSelu: {
+      // activation.rs:236-251: f64 constants, cast to f32 at use.
+      const float alpha = (float)1.6732632423543772, scale = (float)1.0507009873554805;
+      return launch_map(OpSelu{alpha, scale}, in, out, n, s);
+    }
+    case kMish: return launch_map(OpMish{}, in, out, n, s);
+    case kSoftplus: return launch_map(OpSoftplus{}, in, out, n, s);
+    case kSoftsign: return launch_map(OpSoftsign{}, in, out, n, s);
+    case kAddScalar: return launch_map(OpAddScalar{param}, in, out, n, s);
+    case kMulScalar: return launch_map(OpMulScalar{param}, in, out, n, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_binary(BinaryOp op, float param, const float* a, const float* b, float* out,
+                          size_t n, cudaStream_t s) {
+  In<2> in{{a, b}};
+  switch (op) {
+    case kAdd: return launch_map(OpAdd{}, in, out, n, s);
+    case kSub: return launch_map(OpSub{}, in, out, n, s);
+    case kMul: return launch_map(OpMul{}, in, out, n, s);
+    case kDiv: return launch_map(OpDiv{}, in, out, n, s);
+    case kAddMulScalar: return launch_map(OpAddMulScalar{param}, in, out, n, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_fma(const float* a, const float* b, const float* c, float* out, size_t n,
+                       cudaStream_t s) {
+  In<3> in{{a, b, c}};
+  return launch_map(OpFma{}, in, out, n, s);
+}
+
+// ----------------------------------------------------------------- optimizers
+
+namespace {
+
+// One Adam/AdamW element, in the order of optimizer.rs:293-309 and :413-421.
+__device__ __forceinline__ void adam1(const AdamCoeffs& c, float p, float g, float m, float v,
+                                      float& po, float& mo, float& vo) {
+  const float nm = fadd(fmul(m, c.b1), fmul(g, c.one_minus_b1));
+  const float nv = fadd(fmul(v, c.b2), fmul(fmul(g, g), c.one_minus_b2));
+  const float mh = fdiv(nm, c.bc1);
+  const float vh = fdiv(nv, c.bc2);
+  const float den = fadd(fsqrt(vh), c.eps);
+  float np = fsub(p, fmul(fdiv(mh, den), c.lr));
+  if (c.decay) np = fsub(np, fmul(p, c.lr_wd));
+  po = np;
+  mo = nm;
+  vo = nv;
+}
+
+template <int U>
+__global__ void __launch_bounds__(kThreads)
+adam_vec_kernel(const float* p, const float* g, const float* m, const float* v, float* po,
+                float* mo, float* vo, size_t n, AdamCoeffs c) {
+  const size_t n4 = n >> 2;
+  const size_t tile = (size_t)kThreads * U;
+  for (size_t base = (size_t)blockIdx.x * tile + threadIdx.x; base < n4;
+       base += (size_t)gridDim.x * tile) {
+    float4 P[U], G[U], M[U], V[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      if (j < n4) {
+        P[u] = ld4(p + 4 * j);
+        G[u] = ld4(g + 4 * j);
+        M[u] = ld4(m + 4 * j);
+        V[u] = ld4(v + 4 * j);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      if (j < n4) {
+        float4 a, b, d;
+        adam1(c, P[u].x, G[u].x, M[u].x, V[u].x, a.x, b.x, d.x);
+        adam1(c, P[u].y, G[u].y, M[u].y, V[u].y, a.y, b.y, d.y);
+        adam1(c, P[u].z, G[u].z, M[u].z, V[u].z, a.z, b.z, d.z);
+        adam1(c, P[u].w, G[u].w, M[u].w, V[u].w, a.w, b.w, d.w);
+        st4(po + 4 * j, a);
+        st4(mo + 4 * j, b);
+        st4(vo + 4 * j, d);
+      }
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const size_t i = (n4 << 2) + threadIdx.x;
+    float a, b, d;
+    adam1(c, p[i], g[i], m[i], v[i], a, b, d);
+    po[i] = a;
+    mo[i] = b;
+    vo[i] = d;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+adam_scalar_kernel(const float* p, const float* g, const float* m, const float* v, float* po,
+                   float* mo, float* vo, size_t n, AdamCoeffs c) {
+  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads) {
+    float a, b, d;
+    adam1(c, p[i], g[i], m[i], v[i], a, b, d);
+    po[i] = a;
+    mo[i] = b;
+    vo[i] = d;
+  }
+}
+
+// optimizer.rs:150-153: v' = v*mom + g; p' = p - v'*lr
+struct SgdMomentum {
+  float lr, mom;
+};
+__global__ void __launch_bounds__(kThreads)
+sgd_momentum_kernel(const float* p, const float* g, const float* vel, float* po, float* vo,
+                    size_t n, SgdMomentum c) {
+  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads) {
+    const float nv = fadd(fmul(vel[i], c.mom), g[i]);
+    po[i] = fsub(p[i], fmul(nv, c.lr));
+    vo[i] = nv;
+  }
+}
+
+// optimizer.rs:72-74: p - g*lr
+struct OpSgd {
+  float lr;
+  RT_HD float operator()(float p, float g) const { return fsub(p, fmul(g, lr)); }
+};
+
+}  // namespace
+
+cudaError_t launch_adam(const float* p, const float* g, const float* m, const float* v,
+                        float* p_out, float* m_out, float* v_out, size_t n, const AdamCoeffs& c,
+                        cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const bool vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) &&
+                   aligned16(p_out) && aligned16(m_out) && aligned16(v_out);
+  if (vec) {
+    constexpr int U = 2;
+    const unsigned grid = grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * U);
+    adam_vec_kernel<U><<<grid, kThreads, 0, s>>>(p, g, m, v, p_out, m_out, v_out, n, c);
+  } else {
+    adam_scalar_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(p, g, m, v, p_out, m_out,
+                                                                    v_out, n, c);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sgd(const float* p, const float* g, float* p_out, size_t n, float lr,
+                       cudaStream_t s) {
+  In<2> in{{p, g}};
+  return launch_map(OpSgd{lr}, in, p_out, n, s);
+}
+
+cudaError_t launch_sgd_momentum(const float* p, const float* g, const float* vel, float* p_out,
+                                float* vel_out, size_t n, float lr, float momentum,
+                                cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  sgd_momentum_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(p, g, vel, p_out, vel_out, n,
+                                                                  SgdMomentum{lr, momentum});
+  return cudaGetLastError();
+}
+
+}  // namespace rt

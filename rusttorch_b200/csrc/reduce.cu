@@ -1,0 +1,484 @@
+// reduce.cu — global and dim reductions of rusttorch-core (ops/reduction.rs).
+//
+// Global sum/mean/max/min (reduction.rs:7-72).  One HBM pass computes the f64
+// sum and the NaN-ignoring max/min of every block's contiguous share
+// (4 B/element of traffic); a one-block kernel combines the per-block partials
+// in block order, so the result is deterministic for a given device.  The
+// reference folds max/min with partial_cmp (NaN compares Equal, Equal keeps
+// the later element for max and the earlier for min); fmaxf/fminf give the
+// same bits except when a NaN is present or the extreme is a zero, and the
+// host repairs exactly those cases with one more scan (launch_index_scan).
+//
+// Dim reductions (reduction.rs:75-150, plus max along a dim), on a
+// C-contiguous tensor viewed as [outer, len, inner]:
+//  * inner == 1 (the reduced axis is the last one): ndarray reduces each lane
+//    with numeric_util::unrolled_fold — eight strided partial sums combined as
+//    0+(p0+p4), +(p1+p5), +(p2+p6), +(p3+p7), then the tail.  Eight threads
+//    run the eight chains of one lane, each strictly sequential, so the result
+//    is ndarray's bit for bit.  Max uses a warp per lane (order-independent
+//    fmaxf) and re-folds a lane sequentially in the rare NaN/zero case.
+//  * inner > 1: ndarray accumulates `res = res + row` in row order, i.e. each
+//    output is a sequential chain over len.  One thread owns one output
+//    column; a CTA owns a strip of W columns and streams the rows through a
+//    multi-stage cp.async ring in shared memory, so HBM sees fully coalesced
+//    16-byte reads with ~150 KB in flight per SM while every column is still
+//    summed in row order (bit-exact).
+#include "rt_internal.h"
+#include "rt_ops.cuh"
+
+#include <algorithm>
+#include <cfloat>
+
+namespace rt {
+
+namespace {
+
+constexpr int kStatsThreads = 512;
+
+__device__ __forceinline__ double shfl_xor_d(double v, int m) {
+  return __shfl_xor_sync(0xffffffffu, v, m);
+}
+
+struct Acc {
+  double s;
+  float mx, mn;
+  __device__ void init() {
+    s = 0.0;
+    mx = -INFINITY;
+    mn = INFINITY;
+  }
+  __device__ __forceinline__ void add(float v) {
+    s = dadd(s, (double)v);
+    mx = fmaxf(mx, v);
+    mn = fminf(mn, v);
+  }
+  __device__ void merge(const Acc& o) {
+    s = dadd(s, o.s);
+    mx = fmaxf(mx, o.mx);
+    mn = fminf(mn, o.mn);
+  }
+};
+
+// Deterministic block reduction (fixed xor-butterfly and warp order).
+template <int NT>
+__device__ void block_reduce(Acc& a) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    Acc o;
+    o.s = shfl_xor_d(a.s, m);
+    o.mx = __shfl_xor_sync(0xffffffffu, a.mx, m);
+    o.mn = __shfl_xor_sync(0xffffffffu, a.mn, m);
+    a.merge(o);
+  }
+  constexpr int W = NT / 32;
+  __shared__ double ss[W];
+  __shared__ float smx[W], smn[W];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    ss[warp] = a.s;
+    smx[warp] = a.mx;
+    smn[warp] = a.mn;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < W) {
+      a.s = ss[lane];
+      a.mx = smx[lane];
+      a.mn = smn[lane];
+    } else {
+      a.init();
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      Acc o;
+      o.s = shfl_xor_d(a.s, m);
+      o.mx = __shfl_xor_sync(0xffffffffu, a.mx, m);
+      o.mn = __shfl_xor_sync(0xffffffffu, a.mn, m);
+      a.merge(o);
+    }
+  }
+}
+
+// Block b reduces the contiguous element range [b*chunk, (b+1)*chunk) with
+// 16-byte loads (the unaligned head and the tail are read as scalars).
+__global__ void __launch_bounds__(kStatsThreads)
+stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
+  const size_t lo = (size_t)blockIdx.x * chunk;
+  const size_t hi = min(n, lo + chunk);
+  Acc a;
+  a.init();
+  if (lo < hi) {
+    const float* p = x + lo;
+    const size_t cnt = hi - lo;
+    size_t head = ((16u - (reinterpret_cast<uintptr_t>(p) & 15u)) & 15u) >> 2;
+    if (head > cnt) head = cnt;
+    if (threadIdx.x < head) a.add(__ldcs(p + threadIdx.x));
+    const float4* q = reinterpret_cast<const float4*>(p + head);
+    const size_t n4 = (cnt - head) >> 2;
+    constexpr int U = 4;
+    size_t i = threadIdx.x;
+    for (; i + (U - 1) * kStatsThreads < n4; i += U * kStatsThreads) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) v[u] = __ldcs(q + i + u * kStatsThreads);
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        a.add(v[u].x);
+        a.add(v[u].y);
+        a.add(v[u].z);
+        a.add(v[u].w);
+      }
+    }
+    for (; i < n4; i += kStatsThreads) {
+      const float4 v = __ldcs(q + i);
+      a.add(v.x);
+      a.add(v.y);
+      a.add(v.z);
+      a.add(v.w);
+    }
+    const size_t done = head + (n4 << 2);
+    if (threadIdx.x < cnt - done) a.add(__ldcs(p + done + threadIdx.x));
+  }
+  block_reduce<kStatsThreads>(a);
+  if (threadIdx.x == 0) parts[blockIdx.x] = StatsPart{a.s, a.mx, a.mn};
+}
+
+__global__ void __launch_bounds__(kStatsThreads)
+stats_final_kernel(const StatsPart* parts, int nparts, StatsPart* out) {
+  Acc a;
+  a.init();
+  for (int i = threadIdx.x; i < nparts; i += kStatsThreads) {
+    const StatsPart p = parts[i];
+    Acc o;
+    o.s = p.sum;
+    o.mx = p.mx;
+    o.mn = p.mn;
+    a.merge(o);
+  }
+  block_reduce<kStatsThreads>(a);
+  if (threadIdx.x == 0) *out = StatsPart{a.s, a.mx, a.mn};
+}
+
+__global__ void index_scan_init(IndexScan* out) {
+  out->last_nan = 0ull;
+  out->first_zero = ~0ull;
+  out->last_zero = 0ull;
+}
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  return __shfl_xor_sync(0xffffffffu, v, m);
+}
+
+__global__ void __launch_bounds__(kThreads)
+index_scan_kernel(const float* x, size_t n, IndexScan* out) {
+  unsigned long long ln = 0ull, fz = ~0ull, lz = 0ull;
+  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads) {
+    const float v = x[i];
+    const unsigned long long k = (unsigned long long)i + 1ull;
+    if (v != v) ln = k;                 // indices only grow per thread
+    if (v == 0.0f) {
+      if (fz == ~0ull) fz = k;
+      lz = k;
+    }
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    ln = max(ln, shfl_xor_u64(ln, m));
+    fz = min(fz, shfl_xor_u64(fz, m));
+    lz = max(lz, shfl_xor_u64(lz, m));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (ln) atomicMax(&out->last_nan, ln);
+    if (fz != ~0ull) atomicMin(&out->first_zero, fz);
+    if (lz) atomicMax(&out->last_zero, lz);
+  }
+}
+
+// ------------------------------------------------------------ last-axis sum
+// Eight threads per lane: thread j owns ndarray's partial sum p_j over
+// elements j, j+8, j+16, ... of the lane, added strictly in order.  Loads are
+// issued kBatch at a time ahead of the dependent adds.
+constexpr int kLaneThreads = 64;      // 8 lanes per block
+constexpr int kBatch = 32;
+
+__global__ void __launch_bounds__(kLaneThreads)
+lane_sum8_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  const size_t lane = (size_t)blockIdx.x * (kLaneThreads / 8) + (threadIdx.x >> 3);
+  const int j = threadIdx.x & 7;
+  const unsigned gmask = 0xffu << (threadIdx.x & 24);   // this lane's 8 threads
+  float p = 0.0f;
+  const bool active = lane < lanes;
+  const float* base = x + (active ? lane : 0) * len + j;
+  const size_t steps = active ? len / 8 : 0;
+  size_t k = 0;
+  for (; k + kBatch <= steps; k += kBatch) {
+    float buf[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; b++) buf[b] = __ldcs(base + (k + b) * 8);
+#pragma unroll
+    for (int b = 0; b < kBatch; b++) p = fadd(p, buf[b]);
+  }
+  for (; k < steps; k++) p = fadd(p, __ldcs(base + k * 8));
+  // Gather the eight partials on thread j == 0 of the lane.
+  float q[8];
+#pragma unroll
+  for (int t = 0; t < 8; t++) q[t] = __shfl_sync(gmask, p, (threadIdx.x & 24) + t);
+  if (active && j == 0) {
+    float acc = 0.0f;
+    acc = fadd(acc, fadd(q[0], q[4]));
+    acc = fadd(acc, fadd(q[1], q[5]));
+    acc = fadd(acc, fadd(q[2], q[6]));
+    acc = fadd(acc, fadd(q[3], q[7]));
+    const float* lp = x + lane * len;
+    for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, lp[t]);
+    if (mean) acc = fdiv(acc, (float)len);
+    out[lane] = acc;
+  }
+}
+
+// ------------------------------------------------------------ last-axis max
+// Warp per lane.  fmaxf is order-independent; it equals the reference fold
+// unless the lane holds a NaN or its maximum is a zero (+0 and -0 compare
+// Equal, and the fold keeps the last one).  Those lanes are re-folded
+// sequentially by lane 0, which reproduces the reference exactly.
+constexpr int kWarpLaneThreads = 256;
+
+__global__ void __launch_bounds__(kWarpLaneThreads)
+lane_max_kernel(const float* x, size_t lanes, size_t len, float* out) {
+  const size_t lane = (size_t)blockIdx.x * (kWarpLaneThreads / 32) + (threadIdx.x >> 5);
+  if (lane >= lanes) return;
+  const int l = threadIdx.x & 31;
+  const float* p = x + lane * len;
+  float m = -INFINITY;
+  bool nan = false;
+  const bool vec = ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) && (len % 4 == 0);
+  if (vec) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+    const size_t n4 = len / 4;
+    constexpr int U = 4;
+    size_t i = l;
+    for (; i + (U - 1) * 32 < n4; i += U * 32) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) v[u] = __ldcs(q + i + u * 32);
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        nan |= (v[u].x != v[u].x) | (v[u].y != v[u].y) | (v[u].z != v[u].z) | (v[u].w != v[u].w);
+        m = fmaxf(fmaxf(m, v[u].x), fmaxf(v[u].y, fmaxf(v[u].z, v[u].w)));
+      }
+    }
+    for (; i < n4; i += 32) {
+      const float4 v = __ldcs(q + i);
+      nan |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
+      m = fmaxf(fmaxf(m, v.x), fmaxf(v.y, fmaxf(v.z, v.w)));
+    }
+  } else {
+    for (size_t i = l; i < len; i += 32) {
+      const float v = p[i];
+      nan |= (v != v);
+      m = fmaxf(m, v);
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+  nan = __any_sync(0xffffffffu, nan);
+  if (l == 0) {
+    if (nan || m == 0.0f) {
+      float acc = p[0];
+      for (size_t i = 1; i < len; i++) acc = max_fold(acc, p[i]);
+      m = acc;
+    }
+    out[lane] = m;
+  }
+}
+
+// ------------------------------------------------- middle-axis, column strip
+// CTA (o, s) reduces columns [c0, c0+W) of outer slice o over all `len` rows.
+// Rows arrive R at a time through a kStages-deep cp.async ring in shared
+// memory ([kStages][R][W] floats, R sized so the ring stays near kStripSmem).
+constexpr int kStages = 12;
+constexpr int kStripMaxW = 256;
+constexpr size_t kStripSmem = 96 * 1024;   // two CTAs per SM
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <int OP>
+__global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, int W, int R,
+                                    size_t strips, float* out) {
+  extern __shared__ __align__(16) float smem[];
+  const size_t o = blockIdx.x / strips;
+  const size_t s = blockIdx.x % strips;
+  const size_t c0 = s * (size_t)W;
+  const int w_eff = (int)min((size_t)W, inner - c0);
+  const int chunks_per_row = w_eff / 4;           // inner % 4 == 0 and c0 % 4 == 0
+  const float* src = x + o * len * inner + c0;
+  const size_t nstage = (len + R - 1) / R;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const size_t stage_floats = (size_t)R * W;
+
+  auto issue = [&](size_t st) {
+    if (st < nstage) {
+      float* buf = smem + (st % kStages) * stage_floats;
+      const size_t r0 = st * R;
+      const int rows = (int)min((size_t)R, len - r0);
+      for (int t = tid; t < rows * chunks_per_row; t += nt) {
+        const int r = t / chunks_per_row, c = t % chunks_per_row;
+        cp_async16(buf + r * W + 4 * c, src + (r0 + r) * inner + 4 * c);
+      }
+    }
+    cp_async_commit();   // always commit, so group counting stays in step
+  };
+
+  for (int st = 0; st < kStages - 1; st++) issue(st);
+
+  float acc = 0.0f;
+  for (size_t st = 0; st < nstage; st++) {
+    cp_async_wait<kStages - 2>();   // this thread's copies of stage st landed
+    __syncthreads();                // everyone's did; stage st-1 is consumed
+    issue(st + kStages - 1);        // refill the buffer stage st-1 used
+    const float* buf = smem + (st % kStages) * stage_floats;
+    const int rows = (int)min((size_t)R, len - st * R);
+    if (tid < w_eff) {
+      int r = 0;
+      if (OP == kDimMax && st == 0) {
+        acc = buf[tid];               // the fold starts from the first row
+        r = 1;
+      }
+      for (; r < rows; r++) {
+        const float v = buf[r * W + tid];
+        acc = (OP == kDimMax) ? max_fold(acc, v) : fadd(acc, v);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (tid < w_eff) {
+    if (OP == kDimMean) acc = fdiv(acc, (float)len);
+    out[o * inner + c0 + tid] = acc;
+  }
+}
+
+// Any layout: one thread per output, sequential over len (row order).
+template <int OP>
+__global__ void __launch_bounds__(kThreads)
+lane_generic_kernel(const float* x, size_t outer, size_t len, size_t inner, float* out) {
+  const size_t lanes = outer * inner;
+  for (size_t t = (size_t)blockIdx.x * kThreads + threadIdx.x; t < lanes;
+       t += (size_t)gridDim.x * kThreads) {
+    const size_t o = t / inner, i = t % inner;
+    const float* p = x + o * len * inner + i;
+    float acc;
+    size_t l = 0;
+    if (OP == kDimMax) {
+      acc = p[0];
+      l = 1;
+    } else {
+      acc = 0.0f;
+    }
+    for (; l < len; l++) {
+      const float v = p[l * inner];
+      acc = (OP == kDimMax) ? max_fold(acc, v) : fadd(acc, v);
+    }
+    if (OP == kDimMean) acc = fdiv(acc, (float)len);
+    out[t] = acc;
+  }
+}
+
+int cur_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+template <int OP>
+cudaError_t strip_launch(const float* x, size_t outer, size_t len, size_t inner, float* out,
+                         cudaStream_t st) {
+  const int sms = sm_count(cur_device());
+  const size_t target = (size_t)sms * 2;
+  const size_t per_outer = std::max<size_t>(1, (target + outer - 1) / outer);
+  size_t W = (inner + per_outer - 1) / per_outer;
+  W = (W + 3) & ~size_t(3);
+  W = std::min<size_t>(std::max<size_t>(W, 32), kStripMaxW);
+  W = std::min(W, (inner + 3) & ~size_t(3));
+  const size_t strips = (inner + W - 1) / W;
+  const int threads = (int)std::max<size_t>(64, (W + 31) & ~size_t(31));
+  int R = (int)(kStripSmem / ((size_t)kStages * W * sizeof(float)));
+  R = std::max(1, std::min(R, 32));
+  const size_t smem = (size_t)kStages * R * W * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(strip_reduce_kernel<OP>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  strip_reduce_kernel<OP><<<(unsigned)(outer * strips), threads, smem, st>>>(
+      x, len, inner, (int)W, R, strips, out);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int stats_max_parts(int device) { return sm_count(device) * 4; }
+
+int stats_num_parts(int device, size_t n) {
+  // At least ~16K elements per block so that small inputs use few blocks.
+  const size_t want = (n + 16383) / 16384;
+  return (int)std::max<size_t>(1, std::min<size_t>(want, (size_t)stats_max_parts(device)));
+}
+
+cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
+                         cudaStream_t s) {
+  const size_t chunk = (n + (size_t)nparts - 1) / (size_t)nparts;
+  stats_kernel<<<nparts, kStatsThreads, 0, s>>>(x, n, chunk ? chunk : 1, parts);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStream_t s) {
+  index_scan_init<<<1, 1, 0, s>>>(out);
+  const size_t want = (n + kThreads - 1) / kThreads;
+  const unsigned grid =
+      (unsigned)std::max<size_t>(1, std::min<size_t>(want, (size_t)sm_count(cur_device()) * 8));
+  index_scan_kernel<<<grid, kThreads, 0, s>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
+                              size_t inner, float* out, cudaStream_t s) {
+  const size_t lanes = outer * inner;
+  if (lanes == 0) return cudaSuccess;
+  if (inner == 1) {
+    if (op == kDimMax) {
+      const unsigned grid = (unsigned)((lanes + 7) / 8);
+      lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
+    } else {
+      const unsigned grid = (unsigned)((lanes + 7) / 8);
+      lane_sum8_kernel<<<grid, kLaneThreads, 0, s>>>(x, lanes, len, out, op == kDimMean);
+    }
+    return cudaGetLastError();
+  }
+  const bool strip_ok = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && inner % 4 == 0 &&
+                        inner >= 32 && len >= 1;
+  if (strip_ok) {
+    switch (op) {
+      case kDimSum: return strip_launch<kDimSum>(x, outer, len, inner, out, s);
+      case kDimMean: return strip_launch<kDimMean>(x, outer, len, inner, out, s);
+      case kDimMax: return strip_launch<kDimMax>(x, outer, len, inner, out, s);
+    }
+  }
+  const unsigned grid = (unsigned)std::max<size_t>(
+      1, std::min<size_t>((lanes + kThreads - 1) / kThreads, (size_t)sm_count(cur_device()) * 8));
+  switch (op) {
+    case kDimSum: lane_generic_kernel<kDimSum><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out); break;
+    case kDimMean: lane_generic_kernel<kDimMean><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out); break;
+    case kDimMax: lane_generic_kernel<kDimMax><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace rt

@@ -1,0 +1,87 @@
+// rt_internal.h — launchers shared between the kernel files and the C-ABI
+// layer (abi.cu).  Nothing here is exported from the shared library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace rt {
+
+// Threads per block for the streaming kernels.
+constexpr int kThreads = 256;
+
+// Number of SMs of `device` (cached after the first query).
+int sm_count(int device);
+
+// ---------------------------------------------------------------- elementwise
+enum UnaryOp {
+  kRelu, kLeakyRelu, kSigmoid, kTanh, kGelu, kSwish, kElu, kSelu, kMish, kSoftplus, kSoftsign,
+  kAddScalar, kMulScalar,
+};
+enum BinaryOp { kAdd, kSub, kMul, kDiv, kAddMulScalar };
+
+// `param` is alpha (leaky_relu, elu) or the scalar (add/mul_scalar).
+cudaError_t launch_unary(UnaryOp op, float param, const float* x, float* out, size_t n,
+                         cudaStream_t s);
+cudaError_t launch_binary(BinaryOp op, float param, const float* a, const float* b, float* out,
+                          size_t n, cudaStream_t s);
+cudaError_t launch_fma(const float* a, const float* b, const float* c, float* out, size_t n,
+                       cudaStream_t s);
+
+// Coefficients of one Adam/AdamW step, already rounded to f32 on the host
+// exactly as rusttorch-core rounds them (optimizer.rs:278-309, :413-418).
+struct AdamCoeffs {
+  float b1, one_minus_b1, b2, one_minus_b2, bc1, bc2, eps, lr;
+  float lr_wd;      // (f32)(lr*wd) in f64; used only when decay != 0
+  int decay;        // weight_decay > 0
+};
+cudaError_t launch_adam(const float* p, const float* g, const float* m, const float* v,
+                        float* p_out, float* m_out, float* v_out, size_t n, const AdamCoeffs& c,
+                        cudaStream_t s);
+cudaError_t launch_sgd(const float* p, const float* g, float* p_out, size_t n, float lr,
+                       cudaStream_t s);
+cudaError_t launch_sgd_momentum(const float* p, const float* g, const float* vel, float* p_out,
+                                float* vel_out, size_t n, float lr, float momentum,
+                                cudaStream_t s);
+
+// ----------------------------------------------------------------- reductions
+// Per-block partial of the one-pass global statistics.  `mx`/`mn` ignore NaN
+// (fmaxf/fminf); the caller repairs the rare cases in which the reference's
+// fold gives a different bit pattern (NaN present, or a zero extreme).
+struct StatsPart {
+  double sum;
+  float mx;
+  float mn;
+};
+// Blocks used by launch_stats on `device` for n elements (<= stats_max_parts).
+int stats_num_parts(int device, size_t n);
+int stats_max_parts(int device);
+// Writes the combined statistics of x[0..n) to *out (device memory).
+// `parts` is scratch of stats_num_parts(device, n) entries.
+cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
+                         cudaStream_t s);
+
+// Positions used by the exact repair path, 1-based (0 = none).
+struct IndexScan {
+  unsigned long long last_nan;    // last i+1 with x[i] NaN
+  unsigned long long first_zero;  // first i+1 with x[i] == 0 (~0ull = none)
+  unsigned long long last_zero;   // last i+1 with x[i] == 0
+};
+cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStream_t s);
+
+enum DimReduce { kDimSum, kDimMean, kDimMax };
+// Reduce the middle axis of a C-contiguous [outer, len, inner] tensor.
+// inner == 1 is the contiguous-lane (last axis) case.
+cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
+                              size_t inner, float* out, cudaStream_t s);
+
+// -------------------------------------------------------------------- softmax
+cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
+                           cudaStream_t s);
+
+// ------------------------------------------------------------------ generator
+cudaError_t launch_fill(float* out, size_t n, uint64_t seed, uint64_t offset, float a, float b,
+                        int normal, cudaStream_t s);
+
+}  // namespace rt

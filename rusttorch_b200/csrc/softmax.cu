@@ -1,0 +1,229 @@
+// softmax.cu — softmax along a dim (rusttorch-core ops/activation.rs:92-167).
+//
+// Reference, per lane along `dim`:
+//   m = max_by fold (NaN compares Equal), e = exp(x - m), s = sum_axis(e),
+//   y = e / s
+// with ndarray's sum_axis order: the eight-chain unrolled_fold when dim is the
+// last axis, a sequential row-order chain otherwise.
+//
+// Why m may be computed with fmaxf: the fold and fmaxf agree on every lane
+// without NaN except for the sign of a zero maximum, and x - (+0) and x - (-0)
+// round to the same value for every x (x - x is +0 either way), so e is
+// unchanged.  A lane holding a NaN makes e, s and every output NaN under both.
+//
+// Last-axis kernel: one CTA per row.  The row is read once from HBM into
+// shared memory (16-byte loads), exponentiated in place, the eight chains are
+// summed by eight threads in exactly ndarray's order, and y is written once —
+// 8 B/element of traffic, the minimum.  Rows longer than shared memory allows
+// take a four-pass path through the output buffer.
+#include "rt_internal.h"
+#include "rt_ops.cuh"
+
+#include <algorithm>
+
+namespace rt {
+
+namespace {
+
+constexpr int kRowThreads = 256;
+// Largest row kept in shared memory (floats).  Larger rows use the multi-pass
+// path.
+constexpr size_t kMaxSmemRow = 48 * 1024;
+
+__device__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < (int)(blockDim.x >> 5) ? red[l] : -INFINITY;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  v = red[0];
+  __syncthreads();
+  return v;
+}
+
+// ndarray unrolled_fold over e[0..len) (shared memory), run by threads 0..7 of
+// warp 0; returns the sum on thread 0.
+__device__ float chain_sum8(const float* e, size_t len) {
+  const int j = threadIdx.x;          // 0..7
+  const size_t steps = len / 8;
+  float p = 0.0f;
+  for (size_t k = 0; k < steps; k++) p = fadd(p, e[8 * k + j]);
+  float q[8];
+#pragma unroll
+  for (int t = 0; t < 8; t++) q[t] = __shfl_sync(0xffu, p, t);
+  float acc = 0.0f;
+  acc = fadd(acc, fadd(q[0], q[4]));
+  acc = fadd(acc, fadd(q[1], q[5]));
+  acc = fadd(acc, fadd(q[2], q[6]));
+  acc = fadd(acc, fadd(q[3], q[7]));
+  for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, e[t]);
+  return acc;
+}
+
+__global__ void __launch_bounds__(kRowThreads)
+softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
+  extern __shared__ __align__(16) float e[];
+  __shared__ float red[kRowThreads / 32];
+  __shared__ float ssum;
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * len;
+  float* yr = out + row * len;
+  const bool vec = ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(yr)) & 15u) == 0 &&
+                   len % 4 == 0;
+  float m = -INFINITY;
+  if (vec) {
+    const float4* q = reinterpret_cast<const float4*>(xr);
+    float4* es = reinterpret_cast<float4*>(e);
+    for (size_t i = threadIdx.x; i < len / 4; i += kRowThreads) {
+      const float4 v = __ldcs(q + i);
+      es[i] = v;
+      m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+  } else {
+    for (size_t i = threadIdx.x; i < len; i += kRowThreads) {
+      const float v = xr[i];
+      e[i] = v;
+      m = fmaxf(m, v);
+    }
+  }
+  m = block_max(m, red);   // contains __syncthreads: e[] is complete
+  for (size_t i = threadIdx.x; i < len; i += kRowThreads) e[i] = expf_glibc(fsub(e[i], m));
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    const float s = chain_sum8(e, len);
+    if (threadIdx.x == 0) ssum = s;
+  }
+  __syncthreads();
+  const float s = ssum;
+  if (vec) {
+    const float4* es = reinterpret_cast<const float4*>(e);
+    float4* q = reinterpret_cast<float4*>(yr);
+    for (size_t i = threadIdx.x; i < len / 4; i += kRowThreads) {
+      const float4 v = es[i];
+      __stcs(q + i, make_float4(fdiv(v.x, s), fdiv(v.y, s), fdiv(v.z, s), fdiv(v.w, s)));
+    }
+  } else {
+    for (size_t i = threadIdx.x; i < len; i += kRowThreads) yr[i] = fdiv(e[i], s);
+  }
+}
+
+// Long rows, pass 1: m per row (block per row).
+__global__ void __launch_bounds__(kRowThreads)
+row_max_kernel(const float* x, size_t len, float* m_out) {
+  __shared__ float red[kRowThreads / 32];
+  const float* xr = x + (size_t)blockIdx.x * len;
+  float m = -INFINITY;
+  for (size_t i = threadIdx.x; i < len; i += kRowThreads) m = fmaxf(m, xr[i]);
+  m = block_max(m, red);
+  if (threadIdx.x == 0) m_out[blockIdx.x] = m;
+}
+
+// Long rows, pass 2: out = exp(x - m).
+__global__ void __launch_bounds__(kRowThreads)
+row_exp_kernel(const float* x, size_t len, const float* m, float* out) {
+  const size_t row = blockIdx.y;
+  const float mr = m[row];
+  for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < len;
+       i += (size_t)gridDim.x * kRowThreads)
+    out[row * len + i] = expf_glibc(fsub(x[row * len + i], mr));
+}
+
+// Long rows, pass 3: s per row, eight sequential chains (one warp per row).
+__global__ void row_chain_sum_kernel(const float* e, size_t len, float* s_out) {
+  const float* er = e + (size_t)blockIdx.x * len;
+  if (threadIdx.x < 8) {
+    const float s = chain_sum8(er, len);
+    if (threadIdx.x == 0) s_out[blockIdx.x] = s;
+  }
+}
+
+// Long rows, pass 4: out /= s.
+__global__ void __launch_bounds__(kRowThreads)
+row_div_kernel(float* out, size_t len, const float* s) {
+  const size_t row = blockIdx.y;
+  const float sr = s[row];
+  for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < len;
+       i += (size_t)gridDim.x * kRowThreads)
+    out[row * len + i] = fdiv(out[row * len + i], sr);
+}
+
+// dim is not the last axis: one thread per (outer, inner) lane, three passes
+// along len; the sum is ndarray's row-order chain res = res + e_l.
+__global__ void __launch_bounds__(kThreads)
+softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, float* out) {
+  const size_t lanes = outer * inner;
+  for (size_t t = (size_t)blockIdx.x * kThreads + threadIdx.x; t < lanes;
+       t += (size_t)gridDim.x * kThreads) {
+    const size_t o = t / inner, i = t % inner;
+    const float* p = x + o * len * inner + i;
+    float* q = out + o * len * inner + i;
+    float m = -INFINITY;
+    for (size_t l = 0; l < len; l++) m = fmaxf(m, p[l * inner]);
+    float s = 0.0f;
+    for (size_t l = 0; l < len; l++) {
+      const float ev = expf_glibc(fsub(p[l * inner], m));
+      q[l * inner] = ev;
+      s = fadd(s, ev);
+    }
+    for (size_t l = 0; l < len; l++) q[l * inner] = fdiv(q[l * inner], s);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
+                           cudaStream_t s) {
+  if (outer == 0 || len == 0 || inner == 0) return cudaSuccess;
+  if (inner > 1) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t lanes = outer * inner;
+    const unsigned grid = (unsigned)std::max<size_t>(
+        1, std::min<size_t>((lanes + kThreads - 1) / kThreads, (size_t)sm_count(dev) * 8));
+    softmax_lane_kernel<<<grid, kThreads, 0, s>>>(x, outer, len, inner, out);
+    return cudaGetLastError();
+  }
+  const size_t rows = outer;
+  if (len <= kMaxSmemRow) {
+    const size_t smem = len * sizeof(float);
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(softmax_row_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    for (size_t r0 = 0; r0 < rows; r0 += 0x7fffffffull) {
+      const size_t nr = std::min<size_t>(rows - r0, 0x7fffffffull);
+      softmax_row_kernel<<<(unsigned)nr, kRowThreads, smem, s>>>(x + r0 * len, nr, len,
+                                                                 out + r0 * len);
+    }
+    return cudaGetLastError();
+  }
+  // Long rows: m and s per row in stream-ordered scratch.
+  float* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), 2 * rows * sizeof(float), s);
+  if (e != cudaSuccess) return e;
+  float* m = scratch;
+  float* sm = scratch + rows;
+  const unsigned gx = (unsigned)std::min<size_t>((len + kRowThreads - 1) / kRowThreads, 4096);
+  for (size_t r0 = 0; r0 < rows; r0 += 65535) {
+    const unsigned nr = (unsigned)std::min<size_t>(rows - r0, 65535);
+    const float* xr = x + r0 * len;
+    float* yr = out + r0 * len;
+    row_max_kernel<<<nr, kRowThreads, 0, s>>>(xr, len, m + r0);
+    row_exp_kernel<<<dim3(gx, nr), kRowThreads, 0, s>>>(xr, len, m + r0, yr);
+    row_chain_sum_kernel<<<nr, 32, 0, s>>>(yr, len, sm + r0);
+    row_div_kernel<<<dim3(gx, nr), kRowThreads, 0, s>>>(yr, len, sm + r0);
+  }
+  e = cudaGetLastError();
+  cudaFreeAsync(scratch, s);
+  return e;
+}
+
+}  // namespace rt

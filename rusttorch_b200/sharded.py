@@ -1,0 +1,80 @@
+"""Global reductions over a tensor sharded across processes (one per GPU).
+
+Each rank summarises its shard on its own GPU (rtc_shard_summary_local), the
+32-byte summaries are all-gathered with torch.distributed (NCCL over
+NVLink/NVSwitch on GPUs, gloo on CPU), and every rank folds them in rank
+order with rtc_shard_combine, so every rank returns the reference's
+sum/mean/max/min of the concatenated tensor.  That all-gather is the only
+communication of the hot path.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import Structure, c_double, c_float, c_int32, c_uint64
+
+from . import _native as N
+
+
+class ShardSummary(Structure):
+    _fields_ = [("sum", c_double), ("count", c_uint64), ("max", c_float),
+                ("min_nonnan", c_float), ("max_kind", c_int32), ("first_nan", c_int32)]
+
+
+SUMMARY_BYTES = ctypes.sizeof(ShardSummary)
+
+
+def _bind(lib):
+    lib.rtc_shard_summary_local.restype = N.RtcResult
+    lib.rtc_shard_summary_local.argtypes = [ctypes.POINTER(N.RtcTensor),
+                                            ctypes.POINTER(ShardSummary)]
+    lib.rtc_shard_combine.restype = N.RtcResult
+    lib.rtc_shard_combine.argtypes = [ctypes.POINTER(ShardSummary), ctypes.c_size_t,
+                                      ctypes.POINTER(c_double)]
+
+
+def combine(summaries: list[ShardSummary], lib=None) -> tuple[float, float, float, float]:
+    """(sum, mean, max, min) of the concatenation of the shards, in order."""
+    lib = lib or N.lib()
+    _bind(lib)
+    arr = (ShardSummary * max(1, len(summaries)))(*summaries)
+    out = (c_double * 4)()
+    N.check(lib.rtc_shard_combine(arr, len(summaries), out))
+    return tuple(out)
+
+
+class ShardedReducer:
+    """sum/mean/max/min of a tensor sharded over the ranks of the default
+    process group (torch.distributed must be initialised)."""
+
+    def __init__(self, lib, rank: int, world: int):
+        import torch
+
+        self.lib, self.rank, self.world = lib, rank, world
+        _bind(lib)
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        self._send = torch.empty(SUMMARY_BYTES, dtype=torch.uint8, device=dev)
+        self._recv = torch.empty(SUMMARY_BYTES * world, dtype=torch.uint8, device=dev)
+        self._host = torch.empty(SUMMARY_BYTES, dtype=torch.uint8, pin_memory=dev == "cuda")
+
+    def local(self, desc) -> ShardSummary:
+        s = ShardSummary()
+        N.check(self.lib.rtc_shard_summary_local(desc.ref, ctypes.byref(s)))
+        return s
+
+    def exchange(self, s: ShardSummary) -> list[ShardSummary]:
+        import torch.distributed as dist
+
+        ctypes.memmove(self._host.data_ptr(), ctypes.addressof(s), SUMMARY_BYTES)
+        self._send.copy_(self._host, non_blocking=True)
+        dist.all_gather_into_tensor(self._recv, self._send)
+        raw = self._recv.cpu().numpy().tobytes()
+        return [ShardSummary.from_buffer_copy(raw, i * SUMMARY_BYTES) for i in range(self.world)]
+
+    def stats(self, desc) -> tuple[float, float, float, float]:
+        return combine(self.exchange(self.local(desc)), self.lib)
+
+    def sum(self, desc) -> float:
+        return self.stats(desc)[0]
+
+    def close(self) -> None:
+        pass
