@@ -203,7 +203,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops", default=",".join(OPS),
                     help="subset of ops in the step (profiling); the JSON line needs all four")
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: sum 2^26, softmax 8192x4096, adamw 4x2^26 (all > L2)")
     args = ap.parse_args()
+    if args.small:
+        global N2, R4, N5
+        N2, R4, N5 = 1 << 26, 8192, 1 << 26
+        BYTES.update(sum=4 * N2, softmax=8 * R4 * C4, adamw=28 * N5)
+        args.no_e2e = args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args)
         return

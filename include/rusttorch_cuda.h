@@ -24,6 +24,14 @@
  *    per-thread default stream) and calls return once the work is queued,
  *    except the scalar reductions (rtc_sum/mean/max/min, rtc_sharded_*),
  *    which return their value and so wait for it.
+ *  - Host memory: a tensor whose `device` is RTC_HOST_MEMORY lives in host
+ *    memory.  When every tensor of a call does, the op streams the data
+ *    through the calling thread's current GPU (rtc_set_device) in chunks,
+ *    with host-to-device copies, kernels and device-to-host copies of
+ *    consecutive chunks overlapped on three streams, and returns when the
+ *    results are in host memory.  Page-locked memory (rtc_host_alloc) runs at
+ *    full PCIe bandwidth.  Mixing host and device tensors in one call is an
+ *    error.
  *  - dtype: every op implements float32 (RTC_F32).  Other dtypes return
  *    RTC_UNSUPPORTED after the reference's own dtype checks have run.
  */
@@ -39,6 +47,9 @@ extern "C" {
 #endif
 
 #define RTC_VERSION_STRING "0.1.0"
+
+/* rtc_tensor.device value for a tensor in host memory (see Conventions). */
+#define RTC_HOST_MEMORY (-1)
 
 /* dtype codes of CTensorDescriptor.dtype (rusttorch-core/src/ffi/tensor.rs:25) */
 enum { RTC_F32 = 0, RTC_F64 = 1, RTC_I32 = 2, RTC_I64 = 3 };
@@ -94,6 +105,10 @@ void* rtc_get_stream(void);
 /* Waits for the calling thread's stream. */
 rtc_result rtc_synchronize(void);
 int rtc_device_count(void);
+/* The calling thread's current GPU (host-memory ops and the flat *_f32 API
+ * run there). */
+rtc_result rtc_set_device(int device);
+int rtc_get_device(void);
 
 /* Memory helpers for callers without the CUDA runtime (no reference
  * counterpart: the reference owns host memory through ndarray). */

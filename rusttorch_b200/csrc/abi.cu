@@ -10,12 +10,14 @@
 #include "../../include/rusttorch_cuda.h"
 #include "rt_abi_util.h"
 #include "rt_internal.h"
+#include "rt_staging.h"
 
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <vector>
 
 using namespace rt;
 
@@ -58,6 +60,20 @@ extern "C" int rtc_device_count(void) {
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
   return n;
 }
+
+extern "C" rtc_result rtc_set_device(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return backend_error("cudaSetDevice", e);
+  return ok();
+}
+
+extern "C" int rtc_get_device(void) {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+static bool on_host(const rtc_tensor* t) { return t->device == RTC_HOST_MEMORY; }
 
 // ---------------------------------------------------------------- memory
 
@@ -163,6 +179,18 @@ static rtc_result binary(BinaryOp op, float param, const rtc_tensor* a, const rt
   TRY(require_f32(a, context));
   TRY(same_device(a, b, out));
   if (a->numel == 0) return ok();
+  if (on_host(a)) {
+    const std::vector<size_t> iu{4, 4}, ou{4};
+    const std::vector<int> al{-1};
+    return launched(staged_map({a->data, b->data}, iu, {out->data}, ou, al, a->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_binary(op, param, (const float*)din[0],
+                                                      (const float*)din[1], (float*)dout[0], cu, s);
+                               }),
+                    context);
+  }
   DeviceScope scope(a->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_binary(op, param, cf(a), cf(b), f(out), a->numel, thread_stream()),
@@ -217,6 +245,18 @@ extern "C" rtc_result rtc_fused_multiply_add(const rtc_tensor* a, const rtc_tens
   TRY(same_device(a, b, out));
   TRY(same_device(a, c, out));
   if (a->numel == 0) return ok();
+  if (on_host(a)) {
+    const std::vector<size_t> iu{4, 4, 4}, ou{4};
+    const std::vector<int> al{-1};
+    return launched(staged_map({a->data, b->data, c->data}, iu, {out->data}, ou, al, a->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [](const void* const* din, void* const* dout, size_t, size_t cu,
+                                  cudaStream_t s) {
+                                 return launch_fma((const float*)din[0], (const float*)din[1],
+                                                   (const float*)din[2], (float*)dout[0], cu, s);
+                               }),
+                    context);
+  }
   DeviceScope scope(a->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_fma(cf(a), cf(b), cf(c), f(out), a->numel, thread_stream()), context);
@@ -236,6 +276,18 @@ static rtc_result unary(UnaryOp op, float param, const rtc_tensor* x, const rtc_
   TRY(require_f32(x, context));
   TRY(same_device(x, out, out));
   if (x->numel == 0) return ok();
+  if (on_host(x)) {
+    const std::vector<size_t> iu{4}, ou{4};
+    const std::vector<int> al{-1};
+    return launched(staged_map({x->data}, iu, {out->data}, ou, al, x->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_unary(op, param, (const float*)din[0],
+                                                     (float*)dout[0], cu, s);
+                               }),
+                    context);
+  }
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_unary(op, param, cf(x), f(out), x->numel, thread_stream()), context);
@@ -317,6 +369,20 @@ extern "C" rtc_result rtc_softmax(const rtc_tensor* x, size_t dim, const rtc_ten
   if (x->numel == 0) return ok();
   size_t outer, len, inner;
   split_dims(x, dim, &outer, &len, &inner);
+  if (on_host(x)) {
+    // Units are outer slices ([len, inner] each): every lane stays whole.
+    const size_t ub = len * inner * sizeof(float);
+    const std::vector<size_t> iu{ub}, ou{ub};
+    const std::vector<int> al{-1};
+    return launched(staged_map({x->data}, iu, {out->data}, ou, al, outer,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_softmax((const float*)din[0], cu, len, inner,
+                                                       (float*)dout[0], s);
+                               }),
+                    "softmax");
+  }
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_softmax(cf(x), outer, len, inner, f(out), thread_stream()), "softmax");
@@ -339,6 +405,18 @@ static rtc_result reduce_dim(DimReduce op, const rtc_tensor* x, size_t dim, cons
   TRY(require_f32(x, context));
   TRY(same_device(x, out, out));
   if (outer * inner == 0) return ok();
+  if (on_host(x)) {
+    const std::vector<size_t> iu{len * inner * sizeof(float)}, ou{inner * sizeof(float)};
+    const std::vector<int> al{-1};
+    return launched(staged_map({x->data}, iu, {out->data}, ou, al, outer,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_reduce_dim(op, (const float*)din[0], cu, len,
+                                                          inner, (float*)dout[0], s);
+                               }),
+                    context);
+  }
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_reduce_dim(op, cf(x), outer, len, inner, f(out), thread_stream()),
@@ -366,6 +444,18 @@ static rtc_result global(const rtc_tensor* x, const char* op, bool empty_is_erro
     return ok();
   }
   TRY(require_f32(x, op));
+  if (on_host(x)) {
+    std::vector<rtc_shard_summary> parts;
+    cudaError_t e = staged_global_stats(cf(x), x->numel, &parts);
+    if (e != cudaSuccess) return backend_error(op, e);
+    double v[4];
+    combine_summaries(parts.data(), parts.size(), v);
+    st->sum = v[0];
+    st->max = (float)v[2];
+    st->min = (float)v[3];
+    return ok();
+  }
+  if (x->device < 0) return invalid_argument("device", "invalid device ordinal");
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   cudaError_t e = exact_global_stats(cf(x), x->numel, x->device, want, thread_stream(), st);
@@ -443,43 +533,7 @@ extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard
 extern "C" rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]) {
   if (!out) return invalid_argument("out", "must not be null");
   if (n > 0 && !parts) return invalid_argument("parts", "must not be null");
-  double sum = 0.0;
-  uint64_t count = 0;
-  int max_kind = 0;           // 0 identity, 1 max-with, 2 constant
-  float mx = 0.0f;
-  bool min_nan = false, seen = false;
-  float mn = INFINITY;
-  for (size_t i = 0; i < n; i++) {
-    const rtc_shard_summary& p = parts[i];
-    sum += p.sum;
-    count += p.count;
-    if (p.count == 0) continue;
-    if (!seen) {
-      seen = true;
-      min_nan = p.first_nan != 0;   // the first element overall
-      if (min_nan) mn = NAN;
-    }
-    if (p.max_kind == 2) {
-      max_kind = 2;
-      mx = p.max;
-    } else if (p.max_kind == 1) {
-      if (max_kind == 0) {
-        max_kind = 1;
-        mx = p.max;
-      } else {
-        mx = mx > p.max ? mx : p.max;   // Equal keeps the later element
-      }
-    }
-    if (!min_nan) mn = mn > p.min_nonnan ? p.min_nonnan : mn;   // Equal keeps the earlier
-  }
-  out[0] = sum;
-  if (count == 0) {
-    out[1] = out[2] = out[3] = NAN;
-    return empty_tensor("stats");
-  }
-  out[1] = sum / (double)count;
-  out[2] = (double)mx;
-  out[3] = (double)mn;
+  if (!combine_summaries(parts, n, out)) return empty_tensor("stats");
   return ok();
 }
 
@@ -545,6 +599,21 @@ static rtc_result adam_common(const rtc_tensor* p, const rtc_tensor* g, const rt
   c.lr = (float)lr;
   c.decay = adamw && wd > 0.0;
   c.lr_wd = (float)(lr * wd);
+  if (on_host(p)) {
+    const std::vector<size_t> iu{4, 4, 4, 4}, ou{4, 4, 4};
+    const std::vector<int> al{0, 2, 3};   // p', m', v' overwrite p, m, v on the device
+    return launched(staged_map({p->data, g->data, m->data, v->data}, iu,
+                               {po->data, mo->data, vo->data}, ou, al, p->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_adam((const float*)din[0], (const float*)din[1],
+                                                    (const float*)din[2], (const float*)din[3],
+                                                    (float*)dout[0], (float*)dout[1],
+                                                    (float*)dout[2], cu, c, s);
+                               }),
+                    adamw ? "adamw_update" : "adam_update");
+  }
   DeviceScope scope(p->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_adam(cf(p), cf(g), cf(m), cf(v), f(po), f(mo), f(vo), p->numel, c,
@@ -589,6 +658,19 @@ extern "C" rtc_result rtc_sgd_update(const rtc_tensor* p, const rtc_tensor* g, d
   TRY(require_f32(p, "sgd_update"));
   TRY(same_device(p, g, po));
   if (p->numel == 0) return ok();
+  if (on_host(p)) {
+    const std::vector<size_t> iu{4, 4}, ou{4};
+    const std::vector<int> al{0};
+    const float flr = (float)lr;
+    return launched(staged_map({p->data, g->data}, iu, {po->data}, ou, al, p->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_sgd((const float*)din[0], (const float*)din[1],
+                                                   (float*)dout[0], cu, flr, s);
+                               }),
+                    "sgd_update");
+  }
   DeviceScope scope(p->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_sgd(cf(p), cf(g), f(po), p->numel, (float)lr, thread_stream()),
@@ -620,6 +702,21 @@ extern "C" rtc_result rtc_sgd_momentum_update(const rtc_tensor* p, const rtc_ten
   TRY(same_device(p, g, vel));
   TRY(same_device(p, po, vo));
   if (p->numel == 0) return ok();
+  if (on_host(p)) {
+    const std::vector<size_t> iu{4, 4, 4}, ou{4, 4};
+    const std::vector<int> al{0, 2};
+    const float flr = (float)lr, fm = (float)momentum;
+    return launched(staged_map({p->data, g->data, vel->data}, iu, {po->data, vo->data}, ou, al,
+                               p->numel, staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_sgd_momentum(
+                                     (const float*)din[0], (const float*)din[1],
+                                     (const float*)din[2], (float*)dout[0], (float*)dout[1], cu,
+                                     flr, fm, s);
+                               }),
+                    "sgd_momentum_update");
+  }
   DeviceScope scope(p->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   return launched(launch_sgd_momentum(cf(p), cf(g), cf(vel), f(po), f(vo), p->numel, (float)lr,

@@ -202,9 +202,13 @@ rtc_result require_f32(const rtc_tensor* t, const char* context) {
 }
 
 rtc_result same_device(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* c) {
+  const bool ha = a->device == RTC_HOST_MEMORY, hb = b->device == RTC_HOST_MEMORY,
+             hc = c->device == RTC_HOST_MEMORY;
+  if (ha != hb || ha != hc)
+    return invalid_argument("device", "host-memory and device tensors cannot be mixed in one call");
   if (a->device != b->device || a->device != c->device)
     return invalid_argument("device", "all tensors of one call must be on the same device");
-  if (a->device < 0) return invalid_argument("device", "device ordinal must be >= 0");
+  if (a->device < RTC_HOST_MEMORY) return invalid_argument("device", "invalid device ordinal");
   return ok();
 }
 
