@@ -36,6 +36,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "HBM GB/s (% of B200 peak) for add/sum/softmax/AdamW at 1/2/4/8 GPUs"
 N1 = 1 << 24                       # cfg1
 N2 = 1 << 28                       # cfg2
+R3, C3 = 8192, 16384               # cfg3
 R4, C4 = 32768, 4096               # cfg4
 N5 = 1 << 30                       # cfg5
 ADAMW = (1e-3, 0.9, 0.999, 1e-8, 0.01, 10)
@@ -82,7 +83,7 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-i", str(self.gpu), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -196,25 +197,31 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops", default=",".join(OPS),
                     help="subset of ops in the step (profiling); the JSON line needs all four")
+    ap.add_argument("--suite", action="store_true",
+                    help="time every op of every config alone (L2 flushed between runs); "
+                         "prints one JSON line per op")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: sum 2^26, softmax 8192x4096, adamw 4x2^26 (all > L2)")
     args = ap.parse_args()
     if args.small:
-        global N2, R4, N5
-        N2, R4, N5 = 1 << 26, 8192, 1 << 26
+        global N2, R3, R4, N5
+        N2, R3, R4, N5 = 1 << 26, 2048, 8192, 1 << 26
         BYTES.update(sum=4 * N2, softmax=8 * R4 * C4, adamw=28 * N5)
         args.no_e2e = args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args)
         return
     args.warmup = max(args.warmup, 3)
+    if args.suite:
+        run_suite(args)
+        return
 
     import torch
     import torch.distributed as dist
@@ -274,20 +281,18 @@ def main() -> None:
             D[k] = desc(bufs[k], [N5])
     torch.cuda.synchronize()
 
-    sum_out = c_double()
-    sharded = None
-    if world > 1 and "sum" in ops:
-        from rusttorch_b200 import sharded as sh
-        sharded = sh.ShardedReducer(lib, rank, world)
+    # The sum lands in device memory without a host round trip; at N > 1 the
+    # f64 partials are all-gathered over NCCL (the hot path's only exchange).
+    sum_dev = torch.zeros(1, dtype=torch.float64, device="cuda")
+    sum_all = torch.zeros(world, dtype=torch.float64, device="cuda")
 
     def run_op(op):
         if op == "add_mul_scalar":
             N.check(lib.rtc_add_mul_scalar(D["a"].ref, D["b"].ref, 0.5, D["c"].ref))
         elif op == "sum":
-            if sharded is None:
-                N.check(lib.rtc_sum(D["x2"].ref, byref(sum_out)))
-            else:
-                sum_out.value = sharded.sum(D["x2"])
+            N.check(lib.rtc_sum_device(D["x2"].ref, c_void_p(sum_dev.data_ptr())))
+            if world > 1:
+                dist.all_gather_into_tensor(sum_all, sum_dev)
         elif op == "softmax":
             N.check(lib.rtc_softmax(D["x4"].ref, 1, D["y4"].ref))
         elif op == "adamw":
@@ -348,9 +353,6 @@ def main() -> None:
                 traffic = int(parts[1])
     gpu_launches = args.steps * sum({"add_mul_scalar": 1, "sum": 2, "softmax": 1,
                                      "adamw": 1}[o] for o in ops)
-    if sharded is not None:
-        gpu_launches = args.steps * sum({"add_mul_scalar": 1, "sum": 2, "softmax": 1,
-                                         "adamw": 1}[o] for o in ops)
 
     # e2e: the same step through the C ABI from pinned host buffers.
     e2e = None
@@ -389,56 +391,54 @@ def main() -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    if sharded is not None:
-        sharded.close()
     if world > 1:
         dist.destroy_process_group()
 
 
 def run_e2e(args, lib, N, torch, D, bufs, rank, world, stream):
-    """Each step: copy every op's inputs from pinned host memory, run the op
-    through the C ABI, copy its result back (c, the sum, y, and p/m/v)."""
+    """The same step through the C ABI on tensors in pinned host memory
+    (rtc_tensor.device = RTC_HOST_MEMORY): the library streams every op's
+    inputs to the GPU and its results back (c, the sum, y, and p/m/v in
+    place), copies overlapped with the kernels.  Timed on the host clock
+    from the first input byte to the last result byte, max over ranks."""
+    import torch.distributed as dist
+
     k_e2e = max(1, min(args.steps, 3))
+    HOST = -1
     host = {}
-    for k in ("a", "b", "x2", "x4", "p", "g", "m", "v"):
+    for k in ("a", "b", "c", "x2", "x4", "y4", "p", "g", "m", "v"):
         host[k] = torch.empty(bufs[k].numel(), dtype=torch.float32, pin_memory=True)
         host[k].copy_(bufs[k])
-    out = {k: torch.empty(bufs[k].numel(), dtype=torch.float32, pin_memory=True)
-           for k in ("c", "y4")}
-    h2d = sum(host[k].numel() * 4 for k in host)
-    d2h = (out["c"].numel() + out["y4"].numel() + 3 * N5) * 4 + 8
-    sum_out = c_double()
+    torch.cuda.synchronize()
+    shape = {"a": [N1], "b": [N1], "c": [N1], "x2": [N2], "x4": [R4, C4], "y4": [R4, C4],
+             "p": [N5], "g": [N5], "m": [N5], "v": [N5]}
+    H = {k: N.Desc(host[k].data_ptr(), shape[k], N.F32, HOST) for k in host}
+    h2d = sum(host[k].numel() * 4 for k in ("a", "b", "x2", "x4", "p", "g", "m", "v"))
+    d2h = sum(host[k].numel() * 4 for k in ("c", "y4", "p", "m", "v"))
     lr, b1, b2, eps, wd, t = ADAMW
+    reducer = None
+    if world > 1:
+        from rusttorch_b200 import sharded as sh
+        reducer = sh.ShardedReducer(lib, rank, world)
+    out = c_double()
 
     def step():
-        bufs["a"].copy_(host["a"], non_blocking=True)
-        bufs["b"].copy_(host["b"], non_blocking=True)
-        N.check(lib.rtc_add_mul_scalar(D["a"].ref, D["b"].ref, 0.5, D["c"].ref))
-        out["c"].copy_(bufs["c"], non_blocking=True)
-        bufs["x2"].copy_(host["x2"], non_blocking=True)
-        N.check(lib.rtc_sum(D["x2"].ref, byref(sum_out)))
-        bufs["x4"].copy_(host["x4"], non_blocking=True)
-        N.check(lib.rtc_softmax(D["x4"].ref, 1, D["y4"].ref))
-        out["y4"].copy_(bufs["y4"], non_blocking=True)
-        for k in "pgmv":
-            bufs[k].copy_(host[k], non_blocking=True)
-        N.check(lib.rtc_adamw_update(D["p"].ref, D["g"].ref, D["m"].ref, D["v"].ref, lr, b1, b2,
-                                     eps, wd, t, D["p"].ref, D["m"].ref, D["v"].ref))
-        for k in "pmv":
-            host[k].copy_(bufs[k], non_blocking=True)
+        N.check(lib.rtc_add_mul_scalar(H["a"].ref, H["b"].ref, 0.5, H["c"].ref))
+        if reducer is None:
+            N.check(lib.rtc_sum(H["x2"].ref, byref(out)))
+        else:
+            out.value = reducer.stats(H["x2"])[0]
+        N.check(lib.rtc_softmax(H["x4"].ref, 1, H["y4"].ref))
+        N.check(lib.rtc_adamw_update(H["p"].ref, H["g"].ref, H["m"].ref, H["v"].ref, lr, b1, b2,
+                                     eps, wd, t, H["p"].ref, H["m"].ref, H["v"].ref))
 
     step()
-    torch.cuda.synchronize()
-    import torch.distributed as dist
     if world > 1:
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    t0 = time.perf_counter()
     for _ in range(k_e2e):
         step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / k_e2e
+    ms = (time.perf_counter() - t0) * 1e3 / k_e2e
     if world > 1:
         tt = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -446,7 +446,114 @@ def run_e2e(args, lib, N, torch, D, bufs, rank, world, stream):
     value = sum(BYTES.values()) * world / (ms * 1e-3) / 1e9
     return {"value": value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "steps": k_e2e,
-            "path": "pinned host buffers -> cudaMemcpyAsync -> C-ABI op -> cudaMemcpyAsync back"}
+            "path": "C-ABI ops on pinned host tensors (device = RTC_HOST_MEMORY): chunked H2D, "
+                    "kernel and D2H overlapped on three streams inside the library"}
+
+
+def run_suite(args) -> None:
+    """Every op of every BASELINE.json config, timed alone on one GPU: CUDA
+    events around each call, L2 flushed (256 MiB written) before each one,
+    median of max(3, --steps) runs.  One JSON line per op."""
+    import torch
+
+    from rusttorch_b200 import _native as N
+
+    torch.cuda.set_device(0)
+    lib = N.lib()
+    stream = torch.cuda.current_stream()
+    N.check(lib.rtc_set_stream(c_void_p(stream.cuda_stream)))
+    peak, _ = peak_hbm()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+
+    def t(shape):
+        n = 1
+        for d in shape:
+            n *= d
+        x = torch.empty(n, dtype=torch.float32, device="cuda")
+        return x, N.Desc(x.data_ptr(), shape, N.F32, 0)
+
+    def fill(pair, seed, normal=False, a=-1.0, b=1.0):
+        fn = lib.rtc_fill_normal if normal else lib.rtc_fill_uniform
+        N.check(fn(pair[1].ref, seed, 0, a, b))
+
+    def timeit(name, cfg, nbytes, fn):
+        for _ in range(2):
+            fn()
+        times = []
+        for _ in range(max(3, args.steps)):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"op": name, "config": cfg, "ms": ms, "GB_s": gbs,
+                          "frac_of_measured_peak": gbs / peak, "bytes": nbytes}), flush=True)
+
+    lr, b1, b2, eps, wd, tt = ADAMW
+    # cfg1
+    a, b, c = t([N1]), t([N1]), t([N1])
+    fill(a, 1)
+    fill(b, 101)
+    for name, fn in (("add", lib.rtc_add), ("sub", lib.rtc_sub), ("mul", lib.rtc_mul),
+                     ("div", lib.rtc_div)):
+        timeit(name, f"cfg1 [{N1}]", 12 * N1,
+               lambda fn=fn: N.check(fn(a[1].ref, b[1].ref, c[1].ref)))
+    timeit("mul_scalar", f"cfg1 [{N1}]", 8 * N1,
+           lambda: N.check(lib.rtc_mul_scalar(a[1].ref, 0.5, c[1].ref)))
+    timeit("add->mul_scalar (fused)", f"cfg1 [{N1}]", 12 * N1,
+           lambda: N.check(lib.rtc_add_mul_scalar(a[1].ref, b[1].ref, 0.5, c[1].ref)))
+    del a, b, c
+    # cfg2
+    x = t([N2])
+    fill(x, 2, True, 0.0, 1.0)
+    sd = torch.zeros(1, dtype=torch.float64, device="cuda")
+    v = c_double()
+    timeit("sum (device result)", f"cfg2 [{N2}]", 4 * N2,
+           lambda: N.check(lib.rtc_sum_device(x[1].ref, c_void_p(sd.data_ptr()))))
+    for name, fn in (("sum", lib.rtc_sum), ("mean", lib.rtc_mean), ("max", lib.rtc_max),
+                     ("min", lib.rtc_min)):
+        timeit(name + " (host result)", f"cfg2 [{N2}]", 4 * N2,
+               lambda fn=fn: N.check(fn(x[1].ref, byref(v))))
+    del x
+    # cfg3
+    x = t([R3, C3])
+    fill(x, 3)
+    for dim, outn in ((1, R3), (0, C3)):
+        o = t([outn])
+        for name, fn in (("sum_dim", lib.rtc_sum_dim), ("mean_dim", lib.rtc_mean_dim),
+                         ("max_dim", lib.rtc_max_dim)):
+            timeit(f"{name}({dim})", f"cfg3 [{R3},{C3}]", 4 * R3 * C3 + 4 * outn,
+                   lambda fn=fn, o=o, dim=dim: N.check(fn(x[1].ref, dim, o[1].ref)))
+    del x
+    # cfg4
+    x, y = t([R4, C4]), t([R4, C4])
+    fill(x, 4, True, 0.0, 2.0)
+    for name in ("relu", "gelu", "swish", "sigmoid", "tanh", "selu", "softsign", "mish",
+                 "softplus"):
+        fn = getattr(lib, "rtc_" + name)
+        timeit(name, f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+               lambda fn=fn: N.check(fn(x[1].ref, y[1].ref)))
+    timeit("leaky_relu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+           lambda: N.check(lib.rtc_leaky_relu(x[1].ref, y[1].ref, 0.01)))
+    timeit("elu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+           lambda: N.check(lib.rtc_elu(x[1].ref, y[1].ref, 1.0)))
+    timeit("softmax(1)", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+           lambda: N.check(lib.rtc_softmax(x[1].ref, 1, y[1].ref)))
+    del x, y
+    # cfg5
+    P = {k: t([N5]) for k in "pgmv"}
+    fill(P["p"], 51, True, 0.0, 0.02)
+    fill(P["g"], 52, True, 0.0, 1e-2)
+    fill(P["m"], 53, True, 0.0, 1e-3)
+    fill(P["v"], 54, False, 0.0, 1e-4)
+    timeit("adamw (in place)", f"cfg5 4x[{N5}]", 28 * N5,
+           lambda: N.check(lib.rtc_adamw_update(P["p"][1].ref, P["g"][1].ref, P["m"][1].ref,
+                                                P["v"][1].ref, lr, b1, b2, eps, wd, tt,
+                                                P["p"][1].ref, P["m"][1].ref, P["v"][1].ref)))
 
 
 if __name__ == "__main__":

@@ -187,6 +187,10 @@ rtc_result rtc_mean(const rtc_tensor* x, double* out_value);
 rtc_result rtc_max(const rtc_tensor* x, double* out_value);
 /* rusttorch_min, ffi/ops.rs:277-292 -> ops::min, reduction.rs:52-72 */
 rtc_result rtc_min(const rtc_tensor* x, double* out_value);
+/* ops::sum without waiting: queues the sum of the device tensor x on the
+ * calling thread's stream; the f64 result lands in *device_out (device
+ * memory on x's device).  Same value as rtc_sum. */
+rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out);
 /* sum, mean, max and min from one pass over x (no reference counterpart; each
  * value equals the corresponding single op).  out[4] = {sum, mean, max, min}. */
 rtc_result rtc_stats(const rtc_tensor* x, double out[4]);
@@ -238,7 +242,8 @@ typedef struct {
   int32_t first_nan;   /* the shard's first element is NaN */
 } rtc_shard_summary;
 
-/* Summarise one shard (device tensor).  Waits for the result. */
+/* Summarise one shard (a device tensor, or host memory streamed through the
+ * current GPU).  Waits for the result. */
 rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard_summary* out);
 /* Fold n summaries in shard order (host only, no GPU needed).
  * out[4] = {sum, mean, max, min} of the concatenated tensor; an empty total

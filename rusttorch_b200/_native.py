@@ -43,6 +43,13 @@ class RtcResult(Structure):
     _fields_ = [("success", c_bool), ("error_msg", c_void_p), ("code", c_int)]
 
 
+class ShardSummary(Structure):
+    """rtc_shard_summary (include/rusttorch_cuda.h)."""
+    _fields_ = [("sum", c_double), ("count", c_uint64), ("max", c_float),
+                ("min_nonnan", c_float), ("max_kind", ctypes.c_int32),
+                ("first_nan", ctypes.c_int32)]
+
+
 class RusttorchError(ValueError):
     """A failed call.  rusttorch-py maps every TensorError to ValueError
     (rusttorch-py/src/lib.rs:23-25); `code` names the TensorError variant."""
@@ -63,6 +70,8 @@ _SIGNATURES = {
     "rtc_get_stream": (c_void_p, []),
     "rtc_synchronize": (RtcResult, []),
     "rtc_device_count": (c_int, []),
+    "rtc_set_device": (RtcResult, [c_int]),
+    "rtc_get_device": (c_int, []),
     "rtc_malloc": (RtcResult, [c_int, c_size_t, POINTER(c_void_p)]),
     "rtc_free": (RtcResult, [c_int, c_void_p]),
     "rtc_memcpy_h2d": (RtcResult, [c_int, c_void_p, c_void_p, c_size_t]),
@@ -100,6 +109,7 @@ _SIGNATURES = {
     "rtc_max": (RtcResult, [T, POINTER(c_double)]),
     "rtc_min": (RtcResult, [T, POINTER(c_double)]),
     "rtc_stats": (RtcResult, [T, POINTER(c_double)]),
+    "rtc_sum_device": (RtcResult, [T, c_void_p]),
     "rtc_sum_dim": (RtcResult, [T, c_size_t, T]),
     "rtc_mean_dim": (RtcResult, [T, c_size_t, T]),
     "rtc_max_dim": (RtcResult, [T, c_size_t, T]),
@@ -109,6 +119,8 @@ _SIGNATURES = {
                                      c_double, c_uint64, T, T, T]),
     "rtc_sgd_update": (RtcResult, [T, T, c_double, T]),
     "rtc_sgd_momentum_update": (RtcResult, [T, T, T, c_double, c_double, T, T]),
+    "rtc_shard_summary_local": (RtcResult, [T, POINTER(ShardSummary)]),
+    "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
     "rtc_relu_f32": (RtcResult, [c_void_p, c_void_p, c_size_t]),
     "rtc_add_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),
     "rtc_mul_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),

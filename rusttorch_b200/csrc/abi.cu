@@ -495,6 +495,26 @@ extern "C" rtc_result rtc_min(const rtc_tensor* x, double* out_value) {
   return ok();
 }
 
+extern "C" rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out) {
+  TRY(check_desc(x, "input"));
+  if (!device_out) return invalid_argument("device_out", "must not be null");
+  TRY(require_f32(x, "sum"));
+  if (on_host(x) || x->device < 0)
+    return invalid_argument("device", "rtc_sum_device needs a device tensor");
+  DeviceScope scope(x->device);
+  if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+  cudaStream_t s = thread_stream();
+  if (x->numel == 0) return launched(cudaMemsetAsync(device_out, 0, sizeof(double), s), "sum");
+  keep_pool_memory(x->device);
+  const int nparts = stats_num_parts(x->device, x->numel);
+  StatsPart* parts = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&parts), nparts * sizeof(StatsPart), s);
+  if (e != cudaSuccess) return backend_error("sum", e);
+  e = launch_stats(cf(x), x->numel, parts, nparts, nullptr, s, device_out);
+  cudaError_t e2 = cudaFreeAsync(parts, s);
+  return launched(e != cudaSuccess ? e : e2, "sum");
+}
+
 extern "C" rtc_result rtc_stats(const rtc_tensor* x, double out[4]) {
   if (!out) return invalid_argument("out", "must not be null");
   GlobalStats st;
@@ -514,6 +534,14 @@ extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard
   rtc_shard_summary s{};
   s.count = shard->numel;
   s.min_nonnan = INFINITY;
+  if (shard->numel > 0 && on_host(shard)) {
+    TRY(require_f32(shard, "shard_summary"));
+    std::vector<rtc_shard_summary> parts;
+    cudaError_t e = staged_global_stats(cf(shard), shard->numel, &parts);
+    if (e != cudaSuccess) return backend_error("shard_summary", e);
+    *out = compose_summaries(parts.data(), parts.size());
+    return ok();
+  }
   if (shard->numel > 0) {
     GlobalStats st;
     TRY(global(shard, "shard_summary", true, kStatSum | kStatMax | kStatMin, &st));

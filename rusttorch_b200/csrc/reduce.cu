@@ -144,7 +144,7 @@ stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
 }
 
 __global__ void __launch_bounds__(kStatsThreads)
-stats_final_kernel(const StatsPart* parts, int nparts, StatsPart* out) {
+stats_final_kernel(const StatsPart* parts, int nparts, StatsPart* out, double* sum_out) {
   Acc a;
   a.init();
   for (int i = threadIdx.x; i < nparts; i += kStatsThreads) {
@@ -156,7 +156,10 @@ stats_final_kernel(const StatsPart* parts, int nparts, StatsPart* out) {
     a.merge(o);
   }
   block_reduce<kStatsThreads>(a);
-  if (threadIdx.x == 0) *out = StatsPart{a.s, a.mx, a.mn};
+  if (threadIdx.x == 0) {
+    if (out) *out = StatsPart{a.s, a.mx, a.mn};
+    if (sum_out) *sum_out = a.s;
+  }
 }
 
 __global__ void index_scan_init(IndexScan* out) {
@@ -430,12 +433,12 @@ int stats_num_parts(int device, size_t n) {
 }
 
 cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
-                         cudaStream_t s) {
+                         cudaStream_t s, double* sum_out) {
   const size_t chunk = (n + (size_t)nparts - 1) / (size_t)nparts;
   stats_kernel<<<nparts, kStatsThreads, 0, s>>>(x, n, chunk ? chunk : 1, parts);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out);
+  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out, sum_out);
   return cudaGetLastError();
 }
 

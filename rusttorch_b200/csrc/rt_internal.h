@@ -57,10 +57,11 @@ struct StatsPart {
 // Blocks used by launch_stats on `device` for n elements (<= stats_max_parts).
 int stats_num_parts(int device, size_t n);
 int stats_max_parts(int device);
-// Writes the combined statistics of x[0..n) to *out (device memory).
+// Writes the combined statistics of x[0..n) to *out (device memory, may be
+// null) and the sum alone to *sum_out (device memory, may be null).
 // `parts` is scratch of stats_num_parts(device, n) entries.
 cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
-                         cudaStream_t s);
+                         cudaStream_t s, double* sum_out = nullptr);
 
 // Positions used by the exact repair path, 1-based (0 = none).
 struct IndexScan {

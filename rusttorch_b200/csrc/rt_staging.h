@@ -32,6 +32,8 @@ cudaError_t staged_map(const std::vector<const void*>& hin, const std::vector<si
 cudaError_t staged_global_stats(const float* host, size_t n,
                                 std::vector<rtc_shard_summary>* out);
 
+// The summary of the concatenation of n shards, in order.
+rtc_shard_summary compose_summaries(const rtc_shard_summary* parts, size_t n);
 // Folds shard summaries in order (see rtc_shard_combine).  Returns false if
 // the total is empty (out[0] = sum is still written).
 bool combine_summaries(const rtc_shard_summary* parts, size_t n, double out[4]);

@@ -211,44 +211,44 @@ cudaError_t staged_global_stats(const float* host, size_t n,
   return e;
 }
 
-bool combine_summaries(const rtc_shard_summary* parts, size_t n, double out[4]) {
-  double sum = 0.0;
-  uint64_t count = 0;
-  int max_kind = 0;           // 0 identity, 1 max-with, 2 constant
-  float mx = 0.0f;
-  bool min_nan = false, seen = false;
-  float mn = INFINITY;
+// Composition of the shards' fold functions (reduction.rs:36-40, :58-62):
+// for max, a shard holding a NaN restarts the fold (the value after it no
+// longer depends on earlier shards), and Equal keeps the later element; for
+// min, NaN is skipped unless it is the very first element, and Equal keeps
+// the earlier element.
+rtc_shard_summary compose_summaries(const rtc_shard_summary* parts, size_t n) {
+  rtc_shard_summary t{};
+  t.min_nonnan = INFINITY;
   for (size_t i = 0; i < n; i++) {
     const rtc_shard_summary& p = parts[i];
-    sum += p.sum;
-    count += p.count;
+    t.sum += p.sum;
     if (p.count == 0) continue;
-    if (!seen) {
-      seen = true;
-      min_nan = p.first_nan != 0;   // the first element overall
-      if (min_nan) mn = NAN;
+    if (t.count == 0) {
+      t.first_nan = p.first_nan;
+      t.max_kind = p.max_kind;
+      t.max = p.max;
+    } else if (p.max_kind == 2) {
+      t.max_kind = 2;
+      t.max = p.max;
+    } else {
+      t.max = t.max > p.max ? t.max : p.max;
     }
-    if (p.max_kind == 2) {
-      max_kind = 2;                 // a NaN restarts the fold: earlier shards no longer matter
-      mx = p.max;
-    } else if (p.max_kind == 1) {
-      if (max_kind == 0) {
-        max_kind = 1;
-        mx = p.max;
-      } else {
-        mx = mx > p.max ? mx : p.max;   // Equal keeps the later element
-      }
-    }
-    if (!min_nan) mn = mn > p.min_nonnan ? p.min_nonnan : mn;   // Equal keeps the earlier
+    t.min_nonnan = t.min_nonnan > p.min_nonnan ? p.min_nonnan : t.min_nonnan;
+    t.count += p.count;
   }
-  out[0] = sum;
-  if (count == 0) {
+  return t;
+}
+
+bool combine_summaries(const rtc_shard_summary* parts, size_t n, double out[4]) {
+  const rtc_shard_summary t = compose_summaries(parts, n);
+  out[0] = t.sum;
+  if (t.count == 0) {
     out[1] = out[2] = out[3] = NAN;
     return false;
   }
-  out[1] = sum / (double)count;
-  out[2] = (double)mx;
-  out[3] = (double)mn;
+  out[1] = t.sum / (double)t.count;
+  out[2] = (double)t.max;
+  out[3] = t.first_nan ? (double)NAN : (double)t.min_nonnan;
   return true;
 }
 

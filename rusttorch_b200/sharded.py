@@ -10,20 +10,19 @@ communication of the hot path.
 from __future__ import annotations
 
 import ctypes
-from ctypes import Structure, c_double, c_float, c_int32, c_uint64
+from ctypes import c_double
 
 from . import _native as N
 
 
-class ShardSummary(Structure):
-    _fields_ = [("sum", c_double), ("count", c_uint64), ("max", c_float),
-                ("min_nonnan", c_float), ("max_kind", c_int32), ("first_nan", c_int32)]
-
+ShardSummary = N.ShardSummary
 
 SUMMARY_BYTES = ctypes.sizeof(ShardSummary)
 
 
 def _bind(lib):
+    """Binds the two summary entry points on a library loaded elsewhere
+    (N.lib() already binds them)."""
     lib.rtc_shard_summary_local.restype = N.RtcResult
     lib.rtc_shard_summary_local.argtypes = [ctypes.POINTER(N.RtcTensor),
                                             ctypes.POINTER(ShardSummary)]

@@ -45,9 +45,14 @@ def test_every_header_symbol_is_exported():
 
 
 def test_binding_table_covers_header():
-    assert set(N.header_functions()) <= set(N._SIGNATURES) | {
-        n for n in N.header_functions() if n.startswith(("rtc_comm", "rtc_shard", "rtc_host_"))
-        and n not in ("rtc_host_alloc", "rtc_host_free")}
+    assert set(N.header_functions()) <= set(N._SIGNATURES)
+
+
+def test_mixing_host_and_device_is_an_error():
+    host = N.Desc(DUMMY, [4], N.F32, -1)
+    dev = N.Desc(DUMMY, [4], N.F32, 0)
+    code, msg = call("rtc_add", host.ref, dev.ref, host.ref)
+    assert code == N.INVALID_ARGUMENT and "host-memory" in msg
 
 
 def test_add_dtype_checked_before_shape():            # elementwise.rs:15-28
