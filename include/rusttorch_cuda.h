@@ -191,6 +191,18 @@ rtc_result rtc_min(const rtc_tensor* x, double* out_value);
  * calling thread's stream; the f64 result lands in *device_out (device
  * memory on x's device).  Same value as rtc_sum. */
 rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out);
+/* rtc_sum_device for callers that must not allocate GPU memory (no
+ * counterpart in the reference).  rtc_sum_device draws its scratch (one
+ * partial sum per thread block) from the stream-ordered pool; callers whose
+ * GPU memory is already reserved by another allocator, or whose policy or
+ * latency budget rules out allocation, can call this instead: the scratch is
+ * a fixed array inside the library (room for 2048 partials, 32 KB per GPU,
+ * held by every GPU that loads the library until exit).  The first call on a
+ * device looks up that array's device address, so make it before any stream
+ * capture.  Calls share the array: calls that overlap on the GPU race.
+ * Fails with RTC_INVALID_ARGUMENT if x would need more partials than the
+ * array holds (only on GPUs with more than 512 SMs). */
+rtc_result rtc_sum_device_noalloc(const rtc_tensor* x, double* device_out);
 /* sum, mean, max and min from one pass over x (no reference counterpart; each
  * value equals the corresponding single op).  out[4] = {sum, mean, max, min}. */
 rtc_result rtc_stats(const rtc_tensor* x, double out[4]);

@@ -110,6 +110,7 @@ _SIGNATURES = {
     "rtc_min": (RtcResult, [T, POINTER(c_double)]),
     "rtc_stats": (RtcResult, [T, POINTER(c_double)]),
     "rtc_sum_device": (RtcResult, [T, c_void_p]),
+    "rtc_sum_device_noalloc": (RtcResult, [T, c_void_p]),
     "rtc_sum_dim": (RtcResult, [T, c_size_t, T]),
     "rtc_mean_dim": (RtcResult, [T, c_size_t, T]),
     "rtc_max_dim": (RtcResult, [T, c_size_t, T]),
