@@ -115,7 +115,7 @@ stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
     if (threadIdx.x < head) a.add(__ldcs(p + threadIdx.x));
     const float4* q = reinterpret_cast<const float4*>(p + head);
     const size_t n4 = (cnt - head) >> 2;
-    constexpr int U = 4;
+    constexpr int U = 8;
     size_t i = threadIdx.x;
     for (; i + (U - 1) * kStatsThreads < n4; i += U * kStatsThreads) {
       float4 v[U];
@@ -203,7 +203,7 @@ index_scan_kernel(const float* x, size_t n, IndexScan* out) {
 // elements j, j+8, j+16, ... of the lane, added strictly in order.  Loads are
 // issued kBatch at a time ahead of the dependent adds.
 constexpr int kLaneThreads = 64;      // 8 lanes per block
-constexpr int kBatch = 32;
+constexpr int kBatch = 64;
 
 __global__ void __launch_bounds__(kLaneThreads)
 lane_sum8_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
@@ -312,6 +312,10 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Copy slots per thread and stage: a stage holds R*W <= 2048 floats = 512
+// 16-byte chunks, and the CTA has at least 128 threads.
+constexpr int kStripSlots = 4;
+
 template <int OP>
 __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, int W, int R,
                                     size_t strips, float* out) {
@@ -326,15 +330,30 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
   const int tid = threadIdx.x, nt = blockDim.x;
   const size_t stage_floats = (size_t)R * W;
 
+  // The chunks this thread copies are the same in every stage: precompute
+  // their row, shared-memory offset and global offset once.
+  int slot_row[kStripSlots];
+  int slot_soff[kStripSlots];
+  size_t slot_goff[kStripSlots];
+#pragma unroll
+  for (int q = 0; q < kStripSlots; q++) {
+    const int t = tid + q * nt;
+    const int r = chunks_per_row ? t / chunks_per_row : 0;
+    const int c = chunks_per_row ? t % chunks_per_row : 0;
+    slot_row[q] = (t < R * chunks_per_row) ? r : R;   // R = no chunk
+    slot_soff[q] = r * W + 4 * c;
+    slot_goff[q] = (size_t)r * inner + 4 * c;
+  }
+
   auto issue = [&](size_t st) {
     if (st < nstage) {
       float* buf = smem + (st % kStages) * stage_floats;
       const size_t r0 = st * R;
       const int rows = (int)min((size_t)R, len - r0);
-      for (int t = tid; t < rows * chunks_per_row; t += nt) {
-        const int r = t / chunks_per_row, c = t % chunks_per_row;
-        cp_async16(buf + r * W + 4 * c, src + (r0 + r) * inner + 4 * c);
-      }
+      const float* base = src + r0 * inner;
+#pragma unroll
+      for (int q = 0; q < kStripSlots; q++)
+        if (slot_row[q] < rows) cp_async16(buf + slot_soff[q], base + slot_goff[q]);
     }
     cp_async_commit();   // always commit, so group counting stays in step
   };
@@ -354,6 +373,13 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
         acc = buf[tid];               // the fold starts from the first row
         r = 1;
       }
+      for (; r + 8 <= rows; r += 8) {
+        float b[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) b[u] = buf[(r + u) * W + tid];
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc = (OP == kDimMax) ? max_fold(acc, b[u]) : fadd(acc, b[u]);
+      }
       for (; r < rows; r++) {
         const float v = buf[r * W + tid];
         acc = (OP == kDimMax) ? max_fold(acc, v) : fadd(acc, v);
@@ -364,6 +390,89 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
   if (tid < w_eff) {
     if (OP == kDimMean) acc = fdiv(acc, (float)len);
     out[o * inner + c0 + tid] = acc;
+  }
+}
+
+// ------------------------------------------------ last-axis sum, staged
+// The same eight sequential chains per lane as lane_sum8_kernel, but the
+// lanes' bytes arrive through a cp.async ring: a CTA owns kLsRows lanes and
+// streams their columns kLsCols at a time (rows padded by 8 floats so the
+// 8 x kLsRows chain threads read shared memory without bank conflicts).
+// Needs len % 4 == 0 and a 16-byte-aligned base.
+constexpr int kLsRows = 4;
+constexpr int kLsCols = 256;
+constexpr int kLsPitch = kLsCols + 8;
+constexpr int kLsStages = 8;
+constexpr int kLsThreads = 128;
+constexpr int kLsSlots = kLsRows * (kLsCols / 4) / kLsThreads;   // 2 chunks per thread
+
+__global__ void __launch_bounds__(kLsThreads)
+lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  __shared__ __align__(16) float smem[kLsStages][kLsRows][kLsPitch];
+  const size_t lane0 = (size_t)blockIdx.x * kLsRows;
+  const int rows = (int)min((size_t)kLsRows, lanes - lane0);
+  const size_t nstage = (len + kLsCols - 1) / kLsCols;
+  const int tid = threadIdx.x;
+  int slot_r[kLsSlots], slot_c[kLsSlots];
+#pragma unroll
+  for (int q = 0; q < kLsSlots; q++) {
+    const int t = tid + q * kLsThreads;
+    slot_r[q] = t / (kLsCols / 4);
+    slot_c[q] = 4 * (t % (kLsCols / 4));
+  }
+  auto issue = [&](size_t st) {
+    if (st < nstage) {
+      const size_t col0 = st * kLsCols;
+      const int cw = (int)min((size_t)kLsCols, len - col0);
+#pragma unroll
+      for (int q = 0; q < kLsSlots; q++)
+        if (slot_r[q] < rows && slot_c[q] < cw)
+          cp_async16(&smem[st % kLsStages][slot_r[q]][slot_c[q]],
+                     x + (lane0 + slot_r[q]) * len + col0 + slot_c[q]);
+    }
+    cp_async_commit();
+  };
+  for (int st = 0; st < kLsStages - 1; st++) issue(st);
+
+  const int r = tid >> 3, j = tid & 7;          // chain j of lane r (warp 0 only)
+  const bool chain = tid < kLsRows * 8 && r < rows;
+  const size_t steps = len / 8;                 // full groups of eight
+  float p = 0.0f;
+  for (size_t st = 0; st < nstage; st++) {
+    cp_async_wait<kLsStages - 2>();
+    __syncthreads();
+    issue(st + kLsStages - 1);
+    if (chain) {
+      const size_t g0 = st * (kLsCols / 8);     // first group of this stage
+      const int ng = (int)min((size_t)(kLsCols / 8), steps > g0 ? steps - g0 : 0);
+      const float* row = &smem[st % kLsStages][r][j];
+      int u = 0;
+      for (; u + 8 <= ng; u += 8) {
+        float b[8];
+#pragma unroll
+        for (int w = 0; w < 8; w++) b[w] = row[8 * (u + w)];
+#pragma unroll
+        for (int w = 0; w < 8; w++) p = fadd(p, b[w]);
+      }
+      for (; u < ng; u++) p = fadd(p, row[8 * u]);
+    }
+  }
+  cp_async_wait<0>();
+  if (tid < 32) {
+    float q[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) q[t] = __shfl_sync(0xffffffffu, p, (tid & 24) + t);
+    if (chain && j == 0) {
+      float acc = 0.0f;
+      acc = fadd(acc, fadd(q[0], q[4]));
+      acc = fadd(acc, fadd(q[1], q[5]));
+      acc = fadd(acc, fadd(q[2], q[6]));
+      acc = fadd(acc, fadd(q[3], q[7]));
+      const float* lp = x + (lane0 + r) * len;
+      for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, lp[t]);
+      if (mean) acc = fdiv(acc, (float)len);
+      out[lane0 + r] = acc;
+    }
   }
 }
 
@@ -410,9 +519,11 @@ cudaError_t strip_launch(const float* x, size_t outer, size_t len, size_t inner,
   W = std::min<size_t>(std::max<size_t>(W, 32), kStripMaxW);
   W = std::min(W, (inner + 3) & ~size_t(3));
   const size_t strips = (inner + W - 1) / W;
-  const int threads = (int)std::max<size_t>(64, (W + 31) & ~size_t(31));
+  const int threads = (int)std::max<size_t>(128, (W + 31) & ~size_t(31));
   int R = (int)(kStripSmem / ((size_t)kStages * W * sizeof(float)));
   R = std::max(1, std::min(R, 32));
+  // every chunk of a stage needs a copy slot
+  while (R > 1 && (size_t)R * (W / 4) > (size_t)threads * kStripSlots) R--;
   const size_t smem = (size_t)kStages * R * W * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(strip_reduce_kernel<OP>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -459,6 +570,14 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     if (op == kDimMax) {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
       lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
+      const size_t grid = (lanes + kLsRows - 1) / kLsRows;
+      for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+        const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+        lane_sum8_staged_kernel<<<(unsigned)ng, kLsThreads, 0, s>>>(
+            x + g0 * kLsRows * len, lanes - g0 * kLsRows, len, out + g0 * kLsRows,
+            op == kDimMean);
+      }
     } else {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
       lane_sum8_kernel<<<grid, kLaneThreads, 0, s>>>(x, lanes, len, out, op == kDimMean);

@@ -272,21 +272,103 @@ RT_HD float expm1f_glibc(float x) {
   return u2f(f2u(y) + ((uint32_t)k << 23));
 }
 
-// tanhf, bit-identical to glibc's (fdlibm single-precision algorithm).
+// tanhf for 2^-55 <= |x| < 22, without data-dependent branches: fdlibm's
+// tanhf takes t = expm1f(2|x|) (|x| >= 1) or t = expm1f(-2|x|) (|x| < 1), and
+// expm1f picks one of several reconstructions by its reduction count k.  Here
+// every reconstruction the tanh range can reach is evaluated with exactly the
+// operations fdlibm applies on that path, and the one fdlibm would return is
+// selected, so lanes of a warp never diverge; tanh's two final divisions
+// 2/(t+2) and -t/(t+2) share one division.  Bit-identical to tanhf_ref.
+RT_HD float tanhf_common(float x) {
+  const float kLn2Hi = u2f(0x3f317180u), kLn2Lo = u2f(0x3717f7d1u);
+  const float kInvLn2 = u2f(0x3fb8aa3bu);
+  const float kQ1 = u2f(0xbd088889u), kQ2 = u2f(0x3ad00d01u), kQ3 = u2f(0xb8a670cdu);
+  const float kQ4 = u2f(0x36867e54u), kQ5 = u2f(0xb457edbbu);
+  const uint32_t ix = f2u(x) & 0x7fffffffu;
+  const float ax = u2f(ix);
+  const bool ge1 = ix >= 0x3f800000u;
+  // expm1f argument: 2|x| in [2, 44) or -2|x| in (-2, -2^-54].
+  const float a = ge1 ? fmul(2.0f, ax) : fmul(-2.0f, ax);
+  const uint32_t ha = f2u(a) & 0x7fffffffu;
+  const bool aneg = !ge1;
+  // Reduction count: 0 for |a| <= ln2/2, +-1 below 3ln2/2, else truncated
+  // a/ln2 +- 1/2.
+  const int kgen = (int)fadd(fmul(kInvLn2, a), aneg ? -0.5f : 0.5f);
+  const int k = ha <= 0x3eb17218u ? 0 : (ha < 0x3f851592u ? (aneg ? -1 : 1) : kgen);
+  const float tk = (float)k;
+  const float hi = fsub(a, fmul(tk, kLn2Hi));   // k = +-1, 0: a -+ ln2_hi, a
+  const float lo = fmul(tk, kLn2Lo);
+  const float xr = fsub(hi, lo);
+  const float c = fsub(fsub(hi, xr), lo);
+  const float hfx = fmul(0.5f, xr);
+  const float hxs = fmul(xr, hfx);
+  float poly = fadd(kQ4, fmul(hxs, kQ5));
+  poly = fadd(kQ3, fmul(hxs, poly));
+  poly = fadd(kQ2, fmul(hxs, poly));
+  poly = fadd(kQ1, fmul(hxs, poly));
+  const float r1 = fadd(1.0f, fmul(hxs, poly));
+  const float t3 = fsub(3.0f, fmul(r1, hfx));
+  const float e = fmul(hxs, fdiv(fsub(r1, t3), fsub(6.0f, fmul(xr, t3))));
+  // k == 0
+  const float r_k0 = fsub(xr, fsub(fmul(xr, e), hxs));
+  const float e2 = fsub(fsub(fmul(xr, fsub(e, c)), c), hxs);
+  // k == -1 (k == +1 cannot occur: a > 0 only for |x| >= 1, where k >= 3)
+  const float r_km1 = fsub(fmul(0.5f, fsub(xr, e2)), 0.5f);
+  // 2 <= k < 23: (1 - 2^-k) - (e2 - xr);  k <= -2 or k > 56: 1 - (e2 - xr),
+  // then 2^k scaling by exponent add, and -1 for the latter.
+  const uint32_t kbits = (uint32_t)k << 23;
+  const bool small_k = k >= 2 && k < 23;
+  const float one_m = small_k ? u2f(0x3f800000u - (0x1000000u >> (k & 31))) : 1.0f;
+  const float y_ac = u2f(f2u(fsub(one_m, fsub(e2, xr))) + kbits);
+  const float r_c = fsub(y_ac, 1.0f);
+  // 23 <= k <= 56: (xr - (e2 + 2^-k)) + 1, then 2^k scaling.
+  const float two_mk = u2f((uint32_t)((0x7f - k) & 0xff) << 23);
+  const float r_b = u2f(f2u(fadd(fsub(xr, fadd(e2, two_mk)), 1.0f)) + kbits);
+  float t;
+  if (ha < 0x33000000u) t = a;                          // |a| < 2^-25
+  else if (k == 0) t = r_k0;
+  else if (k == -1) t = r_km1;
+  else if (small_k) t = y_ac;
+  else if (k >= 23 && k <= 56) t = r_b;
+  else t = r_c;
+  // tanh = 1 - 2/(t+2) for |x| >= 1, -t/(t+2) below: one division.
+  const float q = fdiv(ge1 ? 2.0f : -t, fadd(t, 2.0f));
+  const float z = ge1 ? fsub(1.0f, q) : q;
+  return (f2u(x) >> 31) ? -z : z;
+}
+
+// tanhf, bit-identical to glibc's (fdlibm single-precision algorithm):
+// the common range through tanhf_common, the rest as fdlibm writes it.
 RT_HD float tanhf_glibc(float x) {
   const uint32_t jx = f2u(x);
   const uint32_t ix = jx & 0x7fffffffu;
+  if (ix < 0x41b00000u && ix >= 0x24000000u) return tanhf_common(x);
   const bool neg = (jx >> 31) != 0;
   if (ix >= 0x7f800000u) {             // +-inf -> +-1, NaN -> NaN
     const float inv = fdiv(1.0f, x);
     return neg ? fsub(inv, 1.0f) : fadd(inv, 1.0f);
   }
+  if (ix >= 0x41b00000u) return neg ? -1.0f : 1.0f;    // |x| >= 22: tanh rounds to +-1
+  if (ix == 0) return x;                               // +-0
+  return fmul(x, fadd(1.0f, x));                       // |x| < 2^-55
+}
+
+// The branching transcription of fdlibm's tanhf, kept as the host-side
+// reference the branch-free version is checked against.
+RT_HD float tanhf_ref(float x) {
+  const uint32_t jx = f2u(x);
+  const uint32_t ix = jx & 0x7fffffffu;
+  const bool neg = (jx >> 31) != 0;
+  if (ix >= 0x7f800000u) {
+    const float inv = fdiv(1.0f, x);
+    return neg ? fsub(inv, 1.0f) : fadd(inv, 1.0f);
+  }
   float z;
-  if (ix < 0x41b00000u) {              // |x| < 22
-    if (ix == 0) return x;             // +-0
-    if (ix < 0x24000000u) return fmul(x, fadd(1.0f, x));   // |x| < 2^-55
+  if (ix < 0x41b00000u) {
+    if (ix == 0) return x;
+    if (ix < 0x24000000u) return fmul(x, fadd(1.0f, x));
     const float ax = u2f(ix);
-    if (ix >= 0x3f800000u) {           // |x| >= 1
+    if (ix >= 0x3f800000u) {
       const float t = expm1f_glibc(fmul(2.0f, ax));
       z = fsub(1.0f, fdiv(2.0f, fadd(t, 2.0f)));
     } else {
@@ -294,12 +376,14 @@ RT_HD float tanhf_glibc(float x) {
       z = fdiv(-t, fadd(t, 2.0f));
     }
   } else {
-    z = 1.0f;                          // |x| >= 22: tanh rounds to +-1
+    z = 1.0f;
   }
   return neg ? -z : z;
 }
 
-// logf rounded once from a double log (see the file comment).
+// logf rounded once from a double log (see the file comment).  A
+// single-precision logf (1 ulp) is not accurate enough: mish amplifies its
+// error past 4 ulp.
 RT_HD float logf_cr(float x) { return (float)log((double)x); }
 
 }  // namespace rt

@@ -49,12 +49,21 @@ __device__ float block_max(float v, float* red) {
 }
 
 // ndarray unrolled_fold over e[0..len) (shared memory), run by threads 0..7 of
-// warp 0; returns the sum on thread 0.
+// warp 0; returns the sum on thread 0.  Each chain is strictly sequential;
+// its shared-memory reads are issued 16 at a time ahead of the adds.
 __device__ float chain_sum8(const float* e, size_t len) {
   const int j = threadIdx.x;          // 0..7
   const size_t steps = len / 8;
   float p = 0.0f;
-  for (size_t k = 0; k < steps; k++) p = fadd(p, e[8 * k + j]);
+  size_t k = 0;
+  for (; k + 16 <= steps; k += 16) {
+    float b[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) b[u] = e[8 * (k + u) + j];
+#pragma unroll
+    for (int u = 0; u < 16; u++) p = fadd(p, b[u]);
+  }
+  for (; k < steps; k++) p = fadd(p, e[8 * k + j]);
   float q[8];
 #pragma unroll
   for (int t = 0; t < 8; t++) q[t] = __shfl_sync(0xffu, p, t);
@@ -112,6 +121,78 @@ softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
   } else {
     for (size_t i = threadIdx.x; i < len; i += kRowThreads) yr[i] = fdiv(e[i], s);
   }
+}
+
+// Rows of up to 512*VPT floats (len % 4 == 0, 16-byte aligned): 128 threads
+// per row, the row held in registers (VPT float4 per thread) from the single
+// load to the single store; shared memory holds only e for the eight chain
+// threads.  Small CTAs let ten or more rows per SM overlap, so one row's
+// sequential chain phase hides behind the other rows' memory traffic.
+constexpr int kRegThreads = 128;
+
+template <int VPT>
+__global__ void __launch_bounds__(kRegThreads)
+softmax_row_reg_kernel(const float* x, size_t len, float* out) {
+  extern __shared__ __align__(16) float e[];
+  __shared__ float red[kRegThreads / 32];
+  __shared__ float ssum;
+  const size_t row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * len);
+  float4* yr = reinterpret_cast<float4*>(out + row * len);
+  float4* es = reinterpret_cast<float4*>(e);
+  const int n4 = (int)(len / 4);
+  float4 v[VPT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = threadIdx.x + i * kRegThreads;
+    if (j < n4) {
+      v[i] = __ldcs(xr + j);
+      m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
+    }
+  }
+  m = block_max(m, red);
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = threadIdx.x + i * kRegThreads;
+    if (j < n4) {
+      v[i].x = expf_glibc(fsub(v[i].x, m));
+      v[i].y = expf_glibc(fsub(v[i].y, m));
+      v[i].z = expf_glibc(fsub(v[i].z, m));
+      v[i].w = expf_glibc(fsub(v[i].w, m));
+      es[j] = v[i];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    const float s = chain_sum8(e, len);
+    if (threadIdx.x == 0) ssum = s;
+  }
+  __syncthreads();
+  const float s = ssum;
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = threadIdx.x + i * kRegThreads;
+    if (j < n4)
+      __stcs(yr + j, make_float4(fdiv(v[i].x, s), fdiv(v[i].y, s), fdiv(v[i].z, s),
+                                 fdiv(v[i].w, s)));
+  }
+}
+
+template <int VPT>
+cudaError_t launch_row_reg(const float* x, size_t rows, size_t len, float* out, cudaStream_t s) {
+  const size_t smem = len * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(softmax_row_reg_kernel<VPT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  for (size_t r0 = 0; r0 < rows; r0 += 0x7fffffffull) {
+    const size_t nr = std::min<size_t>(rows - r0, 0x7fffffffull);
+    softmax_row_reg_kernel<VPT><<<(unsigned)nr, kRegThreads, smem, s>>>(x + r0 * len, len,
+                                                                        out + r0 * len);
+  }
+  return cudaGetLastError();
 }
 
 // Long rows, pass 1: m per row (block per row).
@@ -191,6 +272,13 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
     return cudaGetLastError();
   }
   const size_t rows = outer;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+  if (aligned && len % 4 == 0) {
+    if (len <= 512 * 2) return launch_row_reg<2>(x, rows, len, out, s);
+    if (len <= 512 * 4) return launch_row_reg<4>(x, rows, len, out, s);
+    if (len <= 512 * 8) return launch_row_reg<8>(x, rows, len, out, s);
+    if (len <= 512 * 16) return launch_row_reg<16>(x, rows, len, out, s);
+  }
   if (len <= kMaxSmemRow) {
     const size_t smem = len * sizeof(float);
     if (smem > 48 * 1024) {

@@ -170,7 +170,9 @@ def test_cfg4_softmax_full_size():
 
 @pytest.mark.parametrize("shape,dim", [((3, 5), 1), ((7, 1000), 1), ((50, 6), 0), ((1, 1), 0),
                                        ((4, 5, 6), 0), ((4, 5, 6), 1), ((4, 5, 6), 2),
-                                       ((2, 70001), 1), ((9,), 0), ((6, 4097), 1)])
+                                       ((2, 70001), 1), ((9,), 0), ((6, 4097), 1),
+                                       ((5, 12), 1), ((3, 2052), 1), ((4, 8192), 1),
+                                       ((3, 8196), 1), ((2, 1024), 1)])
 def test_softmax_shapes(shape, dim):
     x = O.normal(int(np.prod(shape)), 42, 0, 3).reshape(shape)
     assert_bits_equal(rt.softmax(dev(x), dim).to_numpy(), O.softmax(x, dim), f"softmax {shape} {dim}")
@@ -267,7 +269,8 @@ def test_cfg3_dim_reductions_full_size(op, dim):
 
 
 @pytest.mark.parametrize("shape", [(13, 37), (5, 1), (1, 5), (3, 40, 36), (2, 3, 4, 5), (17,),
-                                   (6, 1003), (300, 6), (2, 129, 64), (7, 8)])
+                                   (6, 1003), (300, 6), (2, 129, 64), (7, 8), (5, 1004),
+                                   (9, 260), (3, 4096), (1, 65536), (2, 7, 512)])
 @pytest.mark.parametrize("op", ["sum", "mean", "max"])
 def test_dim_reduction_shapes(shape, op):
     x = O.normal(int(np.prod(shape)), 46, 0, 2).reshape(shape)
