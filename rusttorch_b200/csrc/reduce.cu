@@ -300,7 +300,7 @@ lane_max_kernel(const float* x, size_t lanes, size_t len, float* out) {
 // CTA (o, s) reduces columns [c0, c0+W) of outer slice o over all `len` rows.
 // Rows arrive R at a time through a kStages-deep cp.async ring in shared
 // memory ([kStages][R][W] floats, R sized so the ring stays near kStripSmem).
-constexpr int kStages = 12;
+constexpr int kStages = 6;
 constexpr int kStripMaxW = 256;
 constexpr size_t kStripSmem = 96 * 1024;   // two CTAs per SM
 
@@ -312,9 +312,9 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Copy slots per thread and stage: a stage holds R*W <= 2048 floats = 512
+// Copy slots per thread and stage: a stage holds R*W <= 4096 floats = 1024
 // 16-byte chunks, and the CTA has at least 128 threads.
-constexpr int kStripSlots = 4;
+constexpr int kStripSlots = 8;
 
 template <int OP>
 __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, int W, int R,
@@ -360,7 +360,11 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
 
   for (int st = 0; st < kStages - 1; st++) issue(st);
 
-  float acc = 0.0f;
+  // Sums are strictly sequential in row order.  Max keeps fmaxf's value
+  // (order-independent) plus a NaN flag; a column holding a NaN, or whose
+  // maximum is a zero, is re-folded sequentially at the end (rare).
+  float acc = (OP == kDimMax) ? -INFINITY : 0.0f;
+  bool nan = false;
   for (size_t st = 0; st < nstage; st++) {
     cp_async_wait<kStages - 2>();   // this thread's copies of stage st landed
     __syncthreads();                // everyone's did; stage st-1 is consumed
@@ -369,25 +373,39 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
     const int rows = (int)min((size_t)R, len - st * R);
     if (tid < w_eff) {
       int r = 0;
-      if (OP == kDimMax && st == 0) {
-        acc = buf[tid];               // the fold starts from the first row
-        r = 1;
-      }
       for (; r + 8 <= rows; r += 8) {
         float b[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) b[u] = buf[(r + u) * W + tid];
 #pragma unroll
-        for (int u = 0; u < 8; u++) acc = (OP == kDimMax) ? max_fold(acc, b[u]) : fadd(acc, b[u]);
+        for (int u = 0; u < 8; u++) {
+          if (OP == kDimMax) {
+            nan |= b[u] != b[u];
+            acc = fmaxf(acc, b[u]);
+          } else {
+            acc = fadd(acc, b[u]);
+          }
+        }
       }
       for (; r < rows; r++) {
         const float v = buf[r * W + tid];
-        acc = (OP == kDimMax) ? max_fold(acc, v) : fadd(acc, v);
+        if (OP == kDimMax) {
+          nan |= v != v;
+          acc = fmaxf(acc, v);
+        } else {
+          acc = fadd(acc, v);
+        }
       }
     }
   }
   cp_async_wait<0>();
   if (tid < w_eff) {
+    if (OP == kDimMax && (nan || acc == 0.0f)) {
+      const float* col = src + tid;
+      float m = col[0];
+      for (size_t l = 1; l < len; l++) m = max_fold(m, col[l * inner]);
+      acc = m;
+    }
     if (OP == kDimMean) acc = fdiv(acc, (float)len);
     out[o * inner + c0 + tid] = acc;
   }
@@ -402,9 +420,9 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
 constexpr int kLsRows = 4;
 constexpr int kLsCols = 256;
 constexpr int kLsPitch = kLsCols + 8;
-constexpr int kLsStages = 8;
-constexpr int kLsThreads = 128;
-constexpr int kLsSlots = kLsRows * (kLsCols / 4) / kLsThreads;   // 2 chunks per thread
+constexpr int kLsStages = 4;      // ~17 KB: 13 CTAs per SM, one wave for 8192 lanes
+constexpr int kLsThreads = 64;
+constexpr int kLsSlots = kLsRows * (kLsCols / 4) / kLsThreads;   // 4 chunks per thread
 
 __global__ void __launch_bounds__(kLsThreads)
 lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
@@ -521,7 +539,7 @@ cudaError_t strip_launch(const float* x, size_t outer, size_t len, size_t inner,
   const size_t strips = (inner + W - 1) / W;
   const int threads = (int)std::max<size_t>(128, (W + 31) & ~size_t(31));
   int R = (int)(kStripSmem / ((size_t)kStages * W * sizeof(float)));
-  R = std::max(1, std::min(R, 32));
+  R = std::max(1, std::min(R, 64));
   // every chunk of a stage needs a copy slot
   while (R > 1 && (size_t)R * (W / 4) > (size_t)threads * kStripSlots) R--;
   const size_t smem = (size_t)kStages * R * W * sizeof(float);

@@ -26,6 +26,19 @@ namespace rt {
 namespace {
 
 constexpr int kRowThreads = 256;
+
+// e / s for a lane-constant s, without a division per element: with
+// r = 1/s rounded to double, (float)(e * r) equals the IEEE f32 quotient
+// e/s.  Reason: e*r carries a relative error below 2^-51, while the exact
+// quotient of two floats is either representable or at least 2^-49 (relative)
+// away from every midpoint between floats (e - s*m is a nonzero multiple of a
+// unit at most 2^-49 of s*m for a midpoint m), so rounding e*r to f32 lands
+// on the same float.  Checked against IEEE division on 4.2e9 (e, s) pairs
+// with e in [0, 1] (subnormals included) and s in [1, 4096].
+__device__ __forceinline__ double recip_rn(float s) { return __drcp_rn((double)s); }
+__device__ __forceinline__ float div_by(float e, double r) {
+  return __double2float_rn(__dmul_rn((double)e, r));
+}
 // Largest row kept in shared memory (floats).  Larger rows use the multi-pass
 // path.
 constexpr size_t kMaxSmemRow = 48 * 1024;
@@ -110,16 +123,16 @@ softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
     if (threadIdx.x == 0) ssum = s;
   }
   __syncthreads();
-  const float s = ssum;
+  const double r = recip_rn(ssum);
   if (vec) {
     const float4* es = reinterpret_cast<const float4*>(e);
     float4* q = reinterpret_cast<float4*>(yr);
     for (size_t i = threadIdx.x; i < len / 4; i += kRowThreads) {
       const float4 v = es[i];
-      __stcs(q + i, make_float4(fdiv(v.x, s), fdiv(v.y, s), fdiv(v.z, s), fdiv(v.w, s)));
+      __stcs(q + i, make_float4(div_by(v.x, r), div_by(v.y, r), div_by(v.z, r), div_by(v.w, r)));
     }
   } else {
-    for (size_t i = threadIdx.x; i < len; i += kRowThreads) yr[i] = fdiv(e[i], s);
+    for (size_t i = threadIdx.x; i < len; i += kRowThreads) yr[i] = div_by(e[i], r);
   }
 }
 
@@ -169,13 +182,13 @@ softmax_row_reg_kernel(const float* x, size_t len, float* out) {
     if (threadIdx.x == 0) ssum = s;
   }
   __syncthreads();
-  const float s = ssum;
+  const double r = recip_rn(ssum);
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
     const int j = threadIdx.x + i * kRegThreads;
     if (j < n4)
-      __stcs(yr + j, make_float4(fdiv(v[i].x, s), fdiv(v[i].y, s), fdiv(v[i].z, s),
-                                 fdiv(v[i].w, s)));
+      __stcs(yr + j, make_float4(div_by(v[i].x, r), div_by(v[i].y, r), div_by(v[i].z, r),
+                                 div_by(v[i].w, r)));
   }
 }
 
@@ -229,10 +242,10 @@ __global__ void row_chain_sum_kernel(const float* e, size_t len, float* s_out) {
 __global__ void __launch_bounds__(kRowThreads)
 row_div_kernel(float* out, size_t len, const float* s) {
   const size_t row = blockIdx.y;
-  const float sr = s[row];
+  const double r = recip_rn(s[row]);
   for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < len;
        i += (size_t)gridDim.x * kRowThreads)
-    out[row * len + i] = fdiv(out[row * len + i], sr);
+    out[row * len + i] = div_by(out[row * len + i], r);
 }
 
 // dim is not the last axis: one thread per (outer, inner) lane, three passes
@@ -253,7 +266,8 @@ softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, floa
       q[l * inner] = ev;
       s = fadd(s, ev);
     }
-    for (size_t l = 0; l < len; l++) q[l * inner] = fdiv(q[l * inner], s);
+    const double r = recip_rn(s);
+    for (size_t l = 0; l < len; l++) q[l * inner] = div_by(q[l * inner], r);
   }
 }
 
