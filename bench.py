@@ -543,6 +543,10 @@ def run_suite(args) -> None:
            lambda: N.check(lib.rtc_elu(x[1].ref, y[1].ref, 1.0)))
     timeit("softmax(1)", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
            lambda: N.check(lib.rtc_softmax(x[1].ref, 1, y[1].ref)))
+    bias = t([C4])
+    fill(bias, 9)
+    timeit("add_broadcast (row bias)", f"cfg4 [{R4},{C4}] + [{C4}]", 8 * R4 * C4 + 4 * C4,
+           lambda: N.check(lib.rtc_add_broadcast(x[1].ref, bias[1].ref, y[1].ref)))
     del x, y
     # cfg5
     P = {k: t([N5]) for k in "pgmv"}

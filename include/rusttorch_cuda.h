@@ -64,7 +64,8 @@ typedef enum {
   RTC_INVALID_ARGUMENT = 5,  /* TensorError::InvalidArgument   error.rs:46 */
   RTC_SIZE_OVERFLOW = 6,     /* TensorError::SizeOverflow      error.rs:43 */
   RTC_UNSUPPORTED = 7,       /* dtype/layout this library does not implement */
-  RTC_BACKEND_ERROR = 8      /* CUDA or NCCL failure (TensorError::Other, error.rs:66) */
+  RTC_BACKEND_ERROR = 8,     /* CUDA or NCCL failure (TensorError::Other, error.rs:66) */
+  RTC_BROADCAST_ERROR = 9    /* TensorError::BroadcastError    error.rs:36-40 */
 } rtc_status;
 
 /* CTensorDescriptor (rusttorch-core/src/ffi/tensor.rs:13-26) plus the device
@@ -261,6 +262,38 @@ rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard_summary* o
  * out[4] = {sum, mean, max, min} of the concatenated tensor; an empty total
  * writes out[0] = 0 and returns RTC_EMPTY_TENSOR. */
 rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]);
+
+/* -------------------------------------------------------- broadcasting */
+/* ops::add_broadcast / sub_broadcast / mul_broadcast / div_broadcast
+ * (ops/broadcast.rs:177-198): NumPy broadcasting of a and b (dtype checked
+ * first, context "broadcast_tensors"; incompatible shapes give
+ * RTC_BROADCAST_ERROR), then the plain op.  `out` has the broadcast shape.
+ * The operands are read in place through zero strides; nothing is
+ * materialised.  Device tensors only. */
+rtc_result rtc_add_broadcast(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+rtc_result rtc_sub_broadcast(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+rtc_result rtc_mul_broadcast(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+rtc_result rtc_div_broadcast(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out);
+
+/* ------------------------------------------------------- nn optimizers */
+/* nn::Adam::step (nn/optim.rs:262-313) for one parameter: f32
+ * hyperparameters, bias corrections 1 - powf(beta, t) in f32, and the
+ * module's own operation order (it differs from ops::adam_update).  `t` is
+ * the step count after this step's increment (:264); pass zero tensors for
+ * m and v on the first step.  The reference indexes g, m and v by p's length
+ * and panics on a shorter one; here that is RTC_SHAPE_MISMATCH. */
+rtc_result rtc_nn_adam_step(const rtc_tensor* params, const rtc_tensor* grads,
+                            const rtc_tensor* m, const rtc_tensor* v, float lr, float beta1,
+                            float beta2, float eps, uint64_t t, const rtc_tensor* params_out,
+                            const rtc_tensor* m_out, const rtc_tensor* v_out);
+/* nn::SGD::step (nn/optim.rs:148-208) for one parameter.  With momentum > 0
+ * it updates `velocity` (zeros on the first step) into velocity_out;
+ * otherwise velocity and velocity_out may be NULL.  Element counts of params
+ * and grads must match ("SGD step", :160-166). */
+rtc_result rtc_nn_sgd_step(const rtc_tensor* params, const rtc_tensor* grads,
+                           const rtc_tensor* velocity, float lr, float momentum,
+                           float weight_decay, const rtc_tensor* params_out,
+                           const rtc_tensor* velocity_out);
 
 /* ------------------------------------- flat float32 API (device pointers) */
 /* rusttorch_relu_f32 / add_f32 / mul_f32, ffi/ops.rs:348-389: contiguous f32

@@ -537,6 +537,107 @@ int rto_sgd_momentum_update(const float* p, const float* g, const float* vel, si
 }
 
 /* ------------------------------------------------------------------------ */
+/* nn optimizers (core/src/nn/optim.rs)                                     */
+/* ------------------------------------------------------------------------ */
+
+/* Adam::step, nn/optim.rs:262-313: bias corrections in f32 with powf
+ * (:266-268), then per element (:297-304)
+ *   m' = b1*m + (1-b1)*g;  v' = b2*v + ((1-b2)*g)*g
+ *   p' = p - (lr*(m'/bc1)) / (sqrt(v'/bc2) + eps)                          */
+void rto_nn_adam_step(const float* p, const float* g, const float* m, const float* v, size_t n,
+                      float lr, float beta1, float beta2, float eps, uint64_t t, float* p_out,
+                      float* m_out, float* v_out) {
+  const float tf = (float)t;
+  const float bc1 = 1.0f - powf(beta1, tf);
+  const float bc2 = 1.0f - powf(beta2, tf);
+  const float omb1 = 1.0f - beta1, omb2 = 1.0f - beta2;
+  for (size_t j = 0; j < n; j++) {
+    float a = beta1 * m[j];
+    float b = omb1 * g[j];
+    float nm = a + b;
+    float c = beta2 * v[j];
+    float d = omb2 * g[j];
+    d = d * g[j];
+    float nv = c + d;
+    float mh = nm / bc1;
+    float vh = nv / bc2;
+    float num = lr * mh;
+    float den = sqrtf(vh) + eps;
+    float q = num / den;
+    p_out[j] = p[j] - q;
+    m_out[j] = nm;
+    v_out[j] = nv;
+  }
+}
+
+/* SGD::step, nn/optim.rs:168-203:
+ *   momentum > 0: v' = (momentum*v + g) + wd*p;  p' = p - lr*v'
+ *   otherwise:    p' = p - lr*(g + wd*p)                                    */
+void rto_nn_sgd_step(const float* p, const float* g, const float* vel, size_t n, float lr,
+                     float momentum, float weight_decay, float* p_out, float* vel_out) {
+  for (size_t j = 0; j < n; j++) {
+    if (momentum > 0.0f) {
+      float a = momentum * vel[j];
+      a = a + g[j];
+      float b = weight_decay * p[j];
+      float nv = a + b;
+      float step = lr * nv;
+      vel_out[j] = nv;
+      p_out[j] = p[j] - step;
+    } else {
+      float b = weight_decay * p[j];
+      float e = g[j] + b;
+      float step = lr * e;
+      p_out[j] = p[j] - step;
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* broadcasting (core/src/ops/broadcast.rs)                                 */
+/* ------------------------------------------------------------------------ */
+
+/* broadcast_shape (:32-53) then the elementwise op on the materialised
+ * copies (:177-198): element i of the result combines the elements of a and
+ * b at i's coordinates, size-1 (or missing leading) dims repeating. */
+int rto_broadcast_binary(int op, const float* a, const size_t* ashape, size_t andim,
+                         const float* b, const size_t* bshape, size_t bndim, float* out) {
+  enum { MAXD = 16 };
+  size_t nd = andim > bndim ? andim : bndim;
+  if (nd > MAXD) return RTO_INVALID_ARGUMENT;
+  size_t oshape[MAXD], as[MAXD], bs[MAXD];
+  for (size_t i = 0; i < nd; i++) {
+    size_t da = i < nd - andim ? 1 : ashape[i - (nd - andim)];
+    size_t db = i < nd - bndim ? 1 : bshape[i - (nd - bndim)];
+    if (da != db && da != 1 && db != 1) return RTO_BROADCAST_ERROR;
+    oshape[i] = da > db ? da : db;
+    as[i] = da;
+    bs[i] = db;
+  }
+  size_t total = 1;
+  for (size_t i = 0; i < nd; i++) total *= oshape[i];
+  for (size_t idx = 0; idx < total; idx++) {
+    size_t rem = idx, ao = 0, bo = 0, am = 1, bm = 1;
+    for (size_t k = nd; k-- > 0;) {
+      size_t c = rem % oshape[k];
+      rem /= oshape[k];
+      ao += (as[k] == 1 ? 0 : c) * am;
+      bo += (bs[k] == 1 ? 0 : c) * bm;
+      am *= as[k];
+      bm *= bs[k];
+    }
+    float x = a[ao], y = b[bo];
+    switch (op) {
+      case 0: out[idx] = x + y; break;
+      case 1: out[idx] = x - y; break;
+      case 2: out[idx] = x * y; break;
+      default: out[idx] = x / y; break;
+    }
+  }
+  return RTO_OK;
+}
+
+/* ------------------------------------------------------------------------ */
 /* seeded generator                                                         */
 /* ------------------------------------------------------------------------ */
 

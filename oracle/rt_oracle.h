@@ -43,6 +43,7 @@ enum {
   RTO_EMPTY_TENSOR = 3,
   RTO_INVALID_DIMENSION = 4,
   RTO_INVALID_ARGUMENT = 5,
+  RTO_BROADCAST_ERROR = 9,
 };
 
 /* ---- elementwise: core/src/ops/elementwise.rs, core/src/ops/simd.rs ---- */
@@ -90,6 +91,23 @@ int rto_adamw_update(const float* p, const float* g, const float* m, const float
 int rto_sgd_update(const float* p, const float* g, size_t n, double lr, float* p_out);
 int rto_sgd_momentum_update(const float* p, const float* g, const float* vel, size_t n,
                             double lr, double momentum, float* p_out, float* vel_out);
+
+/* ---- nn optimizers: core/src/nn/optim.rs (f32 hyperparameters) ---- */
+/* Adam::step (:262-313) for one parameter; t is the step count after the
+ * increment at :264. */
+void rto_nn_adam_step(const float* p, const float* g, const float* m, const float* v, size_t n,
+                      float lr, float beta1, float beta2, float eps, uint64_t t, float* p_out,
+                      float* m_out, float* v_out);
+/* SGD::step (:148-208) for one parameter; vel/vel_out are used only when
+ * momentum > 0. */
+void rto_nn_sgd_step(const float* p, const float* g, const float* vel, size_t n, float lr,
+                     float momentum, float weight_decay, float* p_out, float* vel_out);
+
+/* ---- broadcasting: core/src/ops/broadcast.rs:55-198 ----
+ * op: 0 add, 1 sub, 2 mul, 3 div.  Returns RTO_BROADCAST_ERROR for shapes
+ * that do not broadcast; out has the broadcast shape. */
+int rto_broadcast_binary(int op, const float* a, const size_t* ashape, size_t andim,
+                         const float* b, const size_t* bshape, size_t bndim, float* out);
 
 /* ---- seeded synthetic inputs (the generator the tests and the CPU baseline
  * use; the CUDA library carries an identical device generator).  Element i of

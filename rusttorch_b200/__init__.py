@@ -26,6 +26,8 @@ __all__ = [
     "softplus", "softsign", "softmax",
     "sum", "mean", "max", "min", "stats", "sum_dim", "mean_dim", "max_dim",
     "adam_update", "adamw_update", "sgd_update", "sgd_momentum_update",
+    "add_broadcast", "sub_broadcast", "mul_broadcast", "div_broadcast",
+    "nn_adam_step", "nn_sgd_step",
     "synchronize",
 ]
 
@@ -263,3 +265,47 @@ def sgd_momentum_update(params, gradients, velocity, learning_rate, momentum):
     check(lib().rtc_sgd_momentum_update(params.desc, gradients.desc, velocity.desc,
                                         float(learning_rate), float(momentum), po.desc, vo.desc))
     return po, vo
+
+
+# ---- broadcasting (rusttorch-py/src/lib.rs:372-398; core ops/broadcast.rs) ----
+def _bshape(a: Tensor, b: Tensor):
+    try:
+        return list(np.broadcast_shapes(tuple(a.shape()), tuple(b.shape())))
+    except ValueError:
+        return a.shape()          # the library reports the BroadcastError
+
+
+def _bcast(fn, a: Tensor, b: Tensor) -> Tensor:
+    out = _like(a, _bshape(a, b))
+    check(fn(a.desc, b.desc, out.desc))
+    return out
+
+
+def add_broadcast(a: Tensor, b: Tensor) -> Tensor: return _bcast(lib().rtc_add_broadcast, a, b)
+def sub_broadcast(a: Tensor, b: Tensor) -> Tensor: return _bcast(lib().rtc_sub_broadcast, a, b)
+def mul_broadcast(a: Tensor, b: Tensor) -> Tensor: return _bcast(lib().rtc_mul_broadcast, a, b)
+def div_broadcast(a: Tensor, b: Tensor) -> Tensor: return _bcast(lib().rtc_div_broadcast, a, b)
+
+
+# ---- nn optimizers (core nn/optim.rs), one parameter per call ---------------
+def nn_adam_step(params, grads, m, v, lr, beta1, beta2, eps, t):
+    """nn::Adam::step for one parameter; t counts steps from 1."""
+    po, mo, vo = _like(params), _like(params), _like(params)
+    check(lib().rtc_nn_adam_step(params.desc, grads.desc, m.desc, v.desc, float(lr),
+                                 float(beta1), float(beta2), float(eps), int(t), po.desc,
+                                 mo.desc, vo.desc))
+    return po, mo, vo
+
+
+def nn_sgd_step(params, grads, velocity, lr, momentum=0.0, weight_decay=0.0):
+    """nn::SGD::step for one parameter; returns (params', velocity')
+    (velocity' is None without momentum)."""
+    po = _like(params)
+    if momentum > 0.0:
+        vo = _like(params)
+        check(lib().rtc_nn_sgd_step(params.desc, grads.desc, velocity.desc, float(lr),
+                                    float(momentum), float(weight_decay), po.desc, vo.desc))
+        return po, vo
+    check(lib().rtc_nn_sgd_step(params.desc, grads.desc, None, float(lr), float(momentum),
+                                float(weight_decay), po.desc, None))
+    return po, None

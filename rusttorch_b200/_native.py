@@ -18,12 +18,12 @@ HEADER_PATH = PKG.parent / "include" / "rusttorch_cuda.h"
 # dtype codes and status codes (rusttorch_cuda.h)
 F32, F64, I32, I64 = 0, 1, 2, 3
 OK, SHAPE_MISMATCH, DTYPE_MISMATCH, EMPTY_TENSOR, INVALID_DIMENSION, INVALID_ARGUMENT, \
-    SIZE_OVERFLOW, UNSUPPORTED, BACKEND_ERROR = range(9)
+    SIZE_OVERFLOW, UNSUPPORTED, BACKEND_ERROR, BROADCAST_ERROR = range(10)
 STATUS_NAMES = {
     OK: "Ok", SHAPE_MISMATCH: "ShapeMismatch", DTYPE_MISMATCH: "DTypeMismatch",
     EMPTY_TENSOR: "EmptyTensor", INVALID_DIMENSION: "InvalidDimension",
     INVALID_ARGUMENT: "InvalidArgument", SIZE_OVERFLOW: "SizeOverflow",
-    UNSUPPORTED: "Unsupported", BACKEND_ERROR: "BackendError",
+    UNSUPPORTED: "Unsupported", BACKEND_ERROR: "BackendError", BROADCAST_ERROR: "BroadcastError",
 }
 
 
@@ -122,6 +122,13 @@ _SIGNATURES = {
     "rtc_sgd_momentum_update": (RtcResult, [T, T, T, c_double, c_double, T, T]),
     "rtc_shard_summary_local": (RtcResult, [T, POINTER(ShardSummary)]),
     "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
+    "rtc_add_broadcast": (RtcResult, [T, T, T]),
+    "rtc_sub_broadcast": (RtcResult, [T, T, T]),
+    "rtc_mul_broadcast": (RtcResult, [T, T, T]),
+    "rtc_div_broadcast": (RtcResult, [T, T, T]),
+    "rtc_nn_adam_step": (RtcResult, [T, T, T, T, c_float, c_float, c_float, c_float, c_uint64,
+                                     T, T, T]),
+    "rtc_nn_sgd_step": (RtcResult, [T, T, T, c_float, c_float, c_float, T, T]),
     "rtc_relu_f32": (RtcResult, [c_void_p, c_void_p, c_size_t]),
     "rtc_add_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),
     "rtc_mul_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),

@@ -565,6 +565,219 @@ extern "C" rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n
   return ok();
 }
 
+// ------------------------------------------------------------ broadcasting
+
+// broadcast_shape (ops/broadcast.rs:32-53) and the plain op on the
+// broadcast operands (:177-198).
+static rtc_result broadcast_op(BinaryOp op, const rtc_tensor* a, const rtc_tensor* b,
+                               const rtc_tensor* out, const char* context, bool float_only,
+                               const char* float_reason) {
+  TRY(check_desc(a, "a"));
+  TRY(check_desc(b, "b"));
+  TRY(check_desc(out, "out"));
+  if (a->dtype != b->dtype)    // broadcast.rs:57-63 (Display form of the dtypes)
+    return dtype_mismatch("broadcast_tensors", dtype_display(a->dtype), dtype_display(b->dtype));
+  if (same_shape(a, b)) return binary(op, 0.f, a, b, out, context, float_only, float_reason);
+  const size_t nd = a->ndim > b->ndim ? a->ndim : b->ndim;
+  std::vector<size_t> os(nd), da(nd), db(nd);
+  for (size_t i = 0; i < nd; i++) {
+    da[i] = i < nd - a->ndim ? 1 : a->shape[i - (nd - a->ndim)];
+    db[i] = i < nd - b->ndim ? 1 : b->shape[i - (nd - b->ndim)];
+    if (da[i] != db[i] && da[i] != 1 && db[i] != 1)
+      return fail(RTC_BROADCAST_ERROR, "Cannot broadcast shapes " + fmt_shape_pub(shape_vec(a)) +
+                                           " and " + fmt_shape_pub(shape_vec(b)) +
+                                           ": Incompatible shapes for broadcasting");
+    os[i] = da[i] > db[i] ? da[i] : db[i];
+  }
+  if (float_only && !is_float(a->dtype)) return invalid_argument("dtype", float_reason);
+  if (shape_vec(out) != os || out->dtype != a->dtype)
+    return shape_mismatch_vec(std::string(context) + " (output)", os, shape_vec(out));
+  TRY(require_f32(a, context));
+  TRY(same_device(a, b, out));
+  if (on_host(a)) return unsupported(std::string(context) + ": broadcast ops need device tensors");
+  if (out->numel == 0) return ok();
+  // Element strides (0 along broadcast dims), then merge dims that continue
+  // each other in both operands.
+  std::vector<long long> sh, as, bs;
+  long long sa = 1, sb = 1;
+  std::vector<long long> fa(nd), fb(nd);
+  for (size_t i = nd; i-- > 0;) {
+    fa[i] = da[i] == 1 ? 0 : sa;
+    fb[i] = db[i] == 1 ? 0 : sb;
+    sa *= (long long)da[i];
+    sb *= (long long)db[i];
+  }
+  for (size_t i = 0; i < nd; i++) {
+    if (os[i] == 1) continue;
+    if (!sh.empty() && as.back() == fa[i] * (long long)os[i] &&
+        bs.back() == fb[i] * (long long)os[i]) {
+      sh.back() *= (long long)os[i];
+      as.back() = fa[i];
+      bs.back() = fb[i];
+    } else {
+      sh.push_back((long long)os[i]);
+      as.push_back(fa[i]);
+      bs.push_back(fb[i]);
+    }
+  }
+  if (sh.empty()) {
+    sh.push_back(1);
+    as.push_back(0);
+    bs.push_back(0);
+  }
+  if (sh.size() > (size_t)kMaxBcastDims)
+    return unsupported(std::string(context) + ": more than 8 non-mergeable broadcast dims");
+  BcastPlan plan{};
+  plan.nd = (int)sh.size();
+  for (int i = 0; i < plan.nd; i++) {
+    plan.shape[i] = sh[i];
+    plan.astride[i] = as[i];
+    plan.bstride[i] = bs[i];
+  }
+  DeviceScope scope(a->device);
+  if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+  return launched(launch_broadcast(op, cf(a), cf(b), f(out), out->numel, plan, thread_stream()),
+                  context);
+}
+
+extern "C" rtc_result rtc_add_broadcast(const rtc_tensor* a, const rtc_tensor* b,
+                                        const rtc_tensor* out) {
+  return broadcast_op(kAdd, a, b, out, "element-wise addition", false, nullptr);
+}
+extern "C" rtc_result rtc_sub_broadcast(const rtc_tensor* a, const rtc_tensor* b,
+                                        const rtc_tensor* out) {
+  return broadcast_op(kSub, a, b, out, "element-wise subtraction", false, nullptr);
+}
+extern "C" rtc_result rtc_mul_broadcast(const rtc_tensor* a, const rtc_tensor* b,
+                                        const rtc_tensor* out) {
+  return broadcast_op(kMul, a, b, out, "element-wise multiplication", false, nullptr);
+}
+extern "C" rtc_result rtc_div_broadcast(const rtc_tensor* a, const rtc_tensor* b,
+                                        const rtc_tensor* out) {
+  return broadcast_op(kDiv, a, b, out, "element-wise division", true,
+                      "Division requires floating-point tensors");
+}
+
+// ---------------------------------------------------------- nn optimizers
+
+extern "C" rtc_result rtc_nn_adam_step(const rtc_tensor* p, const rtc_tensor* g,
+                                       const rtc_tensor* m, const rtc_tensor* v, float lr,
+                                       float beta1, float beta2, float eps, uint64_t t,
+                                       const rtc_tensor* po, const rtc_tensor* mo,
+                                       const rtc_tensor* vo) {
+  TRY(check_desc(p, "params"));
+  TRY(check_desc(g, "gradients"));
+  TRY(check_desc(m, "m"));
+  TRY(check_desc(v, "v"));
+  TRY(check_desc(po, "params_out"));
+  TRY(check_desc(mo, "m_out"));
+  TRY(check_desc(vo, "v_out"));
+  if (g->numel != p->numel) return shape_mismatch("Adam step", p, g);
+  if (m->numel != p->numel) return shape_mismatch("Adam step", p, m);
+  if (v->numel != p->numel) return shape_mismatch("Adam step", p, v);
+  TRY(check_output(p, po, "Adam step"));
+  if (mo->numel != p->numel) return shape_mismatch("Adam step (output)", p, mo);
+  if (vo->numel != p->numel) return shape_mismatch("Adam step (output)", p, vo);
+  TRY(require_f32(p, "Adam step"));
+  TRY(require_f32(g, "Adam step"));
+  TRY(require_f32(m, "Adam step"));
+  TRY(require_f32(v, "Adam step"));
+  TRY(same_device(p, g, m));
+  TRY(same_device(p, v, po));
+  TRY(same_device(p, mo, vo));
+  if (p->numel == 0) return ok();
+  // nn/optim.rs:264-268: t as f32, bias corrections with f32 powf.
+  const float tf = (float)t;
+  NnAdamCoeffs c;
+  c.b1 = beta1;
+  c.one_minus_b1 = 1.0f - beta1;
+  c.b2 = beta2;
+  c.one_minus_b2 = 1.0f - beta2;
+  c.bc1 = 1.0f - powf(beta1, tf);
+  c.bc2 = 1.0f - powf(beta2, tf);
+  c.lr = lr;
+  c.eps = eps;
+  if (on_host(p)) {
+    const std::vector<size_t> iu{4, 4, 4, 4}, ou{4, 4, 4};
+    const std::vector<int> al{0, 2, 3};
+    return launched(staged_map({p->data, g->data, m->data, v->data}, iu,
+                               {po->data, mo->data, vo->data}, ou, al, p->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_nn_adam((const float*)din[0], (const float*)din[1],
+                                                       (const float*)din[2], (const float*)din[3],
+                                                       (float*)dout[0], (float*)dout[1],
+                                                       (float*)dout[2], cu, c, s);
+                               }),
+                    "Adam step");
+  }
+  DeviceScope scope(p->device);
+  if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+  return launched(launch_nn_adam(cf(p), cf(g), cf(m), cf(v), f(po), f(mo), f(vo), p->numel, c,
+                                 thread_stream()),
+                  "Adam step");
+}
+
+extern "C" rtc_result rtc_nn_sgd_step(const rtc_tensor* p, const rtc_tensor* g,
+                                      const rtc_tensor* vel, float lr, float momentum,
+                                      float weight_decay, const rtc_tensor* po,
+                                      const rtc_tensor* vo) {
+  TRY(check_desc(p, "params"));
+  TRY(check_desc(g, "gradients"));
+  TRY(check_desc(po, "params_out"));
+  // nn/optim.rs:160-166 compares element counts.
+  if (p->numel != g->numel) return shape_mismatch("SGD step", p, g);
+  const bool mom = momentum > 0.0f;
+  if (mom) {
+    TRY(check_desc(vel, "velocity"));
+    TRY(check_desc(vo, "velocity_out"));
+    if (vel->numel != p->numel) return shape_mismatch("SGD step", p, vel);
+    if (vo->numel != p->numel) return shape_mismatch("SGD step (output)", p, vo);
+    TRY(require_f32(vel, "SGD step"));
+  }
+  TRY(check_output(p, po, "SGD step"));
+  TRY(require_f32(p, "SGD step"));
+  TRY(require_f32(g, "SGD step"));
+  TRY(same_device(p, g, po));
+  if (mom) TRY(same_device(p, vel, vo));
+  if (p->numel == 0) return ok();
+  if (on_host(p)) {
+    if (mom) {
+      const std::vector<size_t> iu{4, 4, 4}, ou{4, 4};
+      const std::vector<int> al{0, 2};
+      return launched(staged_map({p->data, g->data, vel->data}, iu, {po->data, vo->data}, ou, al,
+                                 p->numel, staged_chunk_units(iu, ou, al),
+                                 [=](const void* const* din, void* const* dout, size_t,
+                                     size_t cu, cudaStream_t s) {
+                                   return launch_nn_sgd((const float*)din[0],
+                                                        (const float*)din[1],
+                                                        (const float*)din[2], (float*)dout[0],
+                                                        (float*)dout[1], cu, lr, momentum,
+                                                        weight_decay, s);
+                                 }),
+                      "SGD step");
+    }
+    const std::vector<size_t> iu{4, 4}, ou{4};
+    const std::vector<int> al{0};
+    return launched(staged_map({p->data, g->data}, iu, {po->data}, ou, al, p->numel,
+                               staged_chunk_units(iu, ou, al),
+                               [=](const void* const* din, void* const* dout, size_t, size_t cu,
+                                   cudaStream_t s) {
+                                 return launch_nn_sgd((const float*)din[0], (const float*)din[1],
+                                                      nullptr, (float*)dout[0], nullptr, cu, lr,
+                                                      momentum, weight_decay, s);
+                               }),
+                    "SGD step");
+  }
+  DeviceScope scope(p->device);
+  if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+  return launched(launch_nn_sgd(cf(p), cf(g), mom ? cf(vel) : nullptr, f(po),
+                                mom ? f(vo) : nullptr, p->numel, lr, momentum, weight_decay,
+                                thread_stream()),
+                  "SGD step");
+}
+
 // ------------------------------------------------------------- optimizers
 
 // optimizer.rs:242-271, in order.  NaN passes (the comparisons are false).

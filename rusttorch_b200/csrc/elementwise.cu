@@ -268,6 +268,73 @@ adam_scalar_kernel(const float* p, const float* g, const float* m, const float* 
   }
 }
 
+// nn/optim.rs:297-304: m' = b1*m + (1-b1)*g; v' = b2*v + ((1-b2)*g)*g;
+// p' = p - (lr*(m'/bc1)) / (sqrt(v'/bc2) + eps)
+__device__ __forceinline__ void nn_adam1(const NnAdamCoeffs& c, float p, float g, float m,
+                                         float v, float& po, float& mo, float& vo) {
+  const float nm = fadd(fmul(c.b1, m), fmul(c.one_minus_b1, g));
+  const float nv = fadd(fmul(c.b2, v), fmul(fmul(c.one_minus_b2, g), g));
+  const float mh = fdiv(nm, c.bc1);
+  const float vh = fdiv(nv, c.bc2);
+  po = fsub(p, fdiv(fmul(c.lr, mh), fadd(fsqrt(vh), c.eps)));
+  mo = nm;
+  vo = nv;
+}
+
+__global__ void __launch_bounds__(kThreads)
+nn_adam_kernel(const float* p, const float* g, const float* m, const float* v, float* po,
+               float* mo, float* vo, size_t n, NnAdamCoeffs c) {
+  const size_t n4 = n >> 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                     reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v) |
+                     reinterpret_cast<uintptr_t>(po) | reinterpret_cast<uintptr_t>(mo) |
+                     reinterpret_cast<uintptr_t>(vo)) & 15u) == 0;
+  if (vec) {
+    for (size_t j = (size_t)blockIdx.x * kThreads + threadIdx.x; j < n4;
+         j += (size_t)gridDim.x * kThreads) {
+      const float4 P = ld4(p + 4 * j), G = ld4(g + 4 * j), M = ld4(m + 4 * j), V = ld4(v + 4 * j);
+      float4 a, b, d;
+      nn_adam1(c, P.x, G.x, M.x, V.x, a.x, b.x, d.x);
+      nn_adam1(c, P.y, G.y, M.y, V.y, a.y, b.y, d.y);
+      nn_adam1(c, P.z, G.z, M.z, V.z, a.z, b.z, d.z);
+      nn_adam1(c, P.w, G.w, M.w, V.w, a.w, b.w, d.w);
+      st4(po + 4 * j, a);
+      st4(mo + 4 * j, b);
+      st4(vo + 4 * j, d);
+    }
+  }
+  const size_t start = vec ? (n4 << 2) : 0;
+  for (size_t i = start + (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads) {
+    float a, b, d;
+    nn_adam1(c, p[i], g[i], m[i], v[i], a, b, d);
+    po[i] = a;
+    mo[i] = b;
+    vo[i] = d;
+  }
+}
+
+// nn/optim.rs:182-190 (momentum > 0): v' = (momentum*v + g) + wd*p; p - lr*v'
+struct NnSgdMomentum {
+  float lr, mom, wd;
+};
+__global__ void __launch_bounds__(kThreads)
+nn_sgd_momentum_kernel(const float* p, const float* g, const float* vel, float* po, float* vo,
+                       size_t n, NnSgdMomentum c) {
+  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * kThreads) {
+    const float nv = fadd(fadd(fmul(c.mom, vel[i]), g[i]), fmul(c.wd, p[i]));
+    vo[i] = nv;
+    po[i] = fsub(p[i], fmul(c.lr, nv));
+  }
+}
+
+// nn/optim.rs:198-203 (no momentum): p - lr*(g + wd*p)
+struct OpNnSgd {
+  float lr, wd;
+  RT_HD float operator()(float p, float g) const { return fsub(p, fmul(lr, fadd(g, fmul(wd, p)))); }
+};
+
 // optimizer.rs:150-153: v' = v*mom + g; p' = p - v'*lr
 struct SgdMomentum {
   float lr, mom;
@@ -306,6 +373,28 @@ cudaError_t launch_adam(const float* p, const float* g, const float* m, const fl
                                                                     v_out, n, c);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_nn_adam(const float* p, const float* g, const float* m, const float* v,
+                           float* p_out, float* m_out, float* v_out, size_t n,
+                           const NnAdamCoeffs& c, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  nn_adam_kernel<<<grid_for(std::max<size_t>(n >> 2, 1), kThreads), kThreads, 0, s>>>(
+      p, g, m, v, p_out, m_out, v_out, n, c);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nn_sgd(const float* p, const float* g, const float* vel, float* p_out,
+                          float* vel_out, size_t n, float lr, float momentum, float wd,
+                          cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if (momentum > 0.0f) {
+    nn_sgd_momentum_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(
+        p, g, vel, p_out, vel_out, n, NnSgdMomentum{lr, momentum, wd});
+    return cudaGetLastError();
+  }
+  In<2> in{{p, g}};
+  return launch_map(OpNnSgd{lr, wd}, in, p_out, n, s);
 }
 
 cudaError_t launch_sgd(const float* p, const float* g, float* p_out, size_t n, float lr,

@@ -37,6 +37,8 @@ static std::string fmt_shape(const std::vector<size_t>& s) {
   return out + "]";
 }
 
+std::string fmt_shape_pub(const std::vector<size_t>& s) { return fmt_shape(s); }
+
 rtc_result shape_mismatch_vec(const std::string& context, const std::vector<size_t>& expected,
                               const std::vector<size_t>& actual) {
   return fail(RTC_SHAPE_MISMATCH, "Shape mismatch in " + context + ": expected " +

@@ -33,6 +33,8 @@ rtc_result launched(cudaError_t e, const char* what);
     if (!_r.success) return _r;        \
   } while (0)
 
+// Rust's `{:?}` of a shape ("[2, 3]").
+std::string fmt_shape_pub(const std::vector<size_t>& s);
 // Rust's `{}` for f64 (shortest round-trip digits, positional notation).
 std::string rust_f64(double v);
 // Rust's `{:?}` (DType::Float32 ...) and `{}` (float32 ...) for a dtype code.

@@ -45,6 +45,33 @@ cudaError_t launch_sgd_momentum(const float* p, const float* g, const float* vel
                                 float* vel_out, size_t n, float lr, float momentum,
                                 cudaStream_t s);
 
+// nn::Adam::step coefficients (core/src/nn/optim.rs:262-313): f32 throughout,
+// bias corrections 1 - powf(beta, t) in f32.
+struct NnAdamCoeffs {
+  float b1, one_minus_b1, b2, one_minus_b2, bc1, bc2, lr, eps;
+};
+cudaError_t launch_nn_adam(const float* p, const float* g, const float* m, const float* v,
+                           float* p_out, float* m_out, float* v_out, size_t n,
+                           const NnAdamCoeffs& c, cudaStream_t s);
+// nn::SGD::step (core/src/nn/optim.rs:148-208); vel/vel_out only when
+// momentum > 0.
+cudaError_t launch_nn_sgd(const float* p, const float* g, const float* vel, float* p_out,
+                          float* vel_out, size_t n, float lr, float momentum, float wd,
+                          cudaStream_t s);
+
+// Broadcast binary op (core/src/ops/broadcast.rs:177-198) on C-contiguous
+// inputs; dims already collapsed: out has shape[0..nd), a and b element
+// strides per dim (0 where broadcast).
+constexpr int kMaxBcastDims = 8;
+struct BcastPlan {
+  int nd;
+  long long shape[kMaxBcastDims];
+  long long astride[kMaxBcastDims];
+  long long bstride[kMaxBcastDims];
+};
+cudaError_t launch_broadcast(BinaryOp op, const float* a, const float* b, float* out,
+                             size_t n, const BcastPlan& plan, cudaStream_t s);
+
 // ----------------------------------------------------------------- reductions
 // Per-block partial of the one-pass global statistics.  `mx`/`mn` ignore NaN
 // (fmaxf/fminf); the caller repairs the rare cases in which the reference's

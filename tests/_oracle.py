@@ -51,6 +51,10 @@ def lib():
             "rto_fill_uniform": (None, [F, c_size_t, c_uint64, c_uint64, c_float, c_float]),
             "rto_fill_normal": (None, [F, c_size_t, c_uint64, c_uint64, c_float, c_float]),
             "rto_set_threads": (None, [c_int]), "rto_get_threads": (c_int, []),
+            "rto_nn_adam_step": (None, [F, F, F, F, c_size_t, c_float, c_float, c_float,
+                                        c_float, c_uint64, F, F, F]),
+            "rto_nn_sgd_step": (None, [F, F, F, c_size_t, c_float, c_float, c_float, F, F]),
+            "rto_broadcast_binary": (c_int, [c_int, F, sz, c_size_t, F, sz, c_size_t, F]),
         }
         for k, (r, a) in sig.items():
             fn = getattr(_lib, k)
@@ -149,3 +153,33 @@ def adam(pp, g, m, v, lr, b1, b2, eps, t):
     rc = lib().rto_adam_update(p(pp), p(g), p(m), p(v), pp.size, lr, b1, b2, eps, t,
                                p(po), p(mo), p(vo))
     return rc, po, mo, vo
+
+
+def broadcast(op, a, b):
+    """op in ("add", "sub", "mul", "div"); returns (rc, out)."""
+    shape = np.broadcast_shapes(a.shape, b.shape) if _bok(a.shape, b.shape) else a.shape
+    out = np.empty(shape, dtype=np.float32)
+    rc = lib().rto_broadcast_binary(["add", "sub", "mul", "div"].index(op), p(a), _shape(a), a.ndim,
+                                    p(b), _shape(b), b.ndim, p(out))
+    return rc, out
+
+
+def _bok(sa, sb):
+    try:
+        np.broadcast_shapes(sa, sb)
+        return True
+    except ValueError:
+        return False
+
+
+def nn_adam(pp, g, m, v, lr, b1, b2, eps, t):
+    po, mo, vo = np.empty_like(pp), np.empty_like(pp), np.empty_like(pp)
+    lib().rto_nn_adam_step(p(pp), p(g), p(m), p(v), pp.size, lr, b1, b2, eps, t, p(po), p(mo), p(vo))
+    return po, mo, vo
+
+
+def nn_sgd(pp, g, vel, lr, momentum, wd):
+    po, vo = np.empty_like(pp), np.empty_like(pp)
+    vel = vel if vel is not None else np.zeros_like(pp)
+    lib().rto_nn_sgd_step(p(pp), p(g), p(vel), pp.size, lr, momentum, wd, p(po), p(vo))
+    return po, vo
