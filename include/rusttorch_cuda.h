@@ -295,6 +295,61 @@ rtc_result rtc_nn_sgd_step(const rtc_tensor* params, const rtc_tensor* grads,
                            float weight_decay, const rtc_tensor* params_out,
                            const rtc_tensor* velocity_out);
 
+/* ---- autograd backward (rusttorch-core src/autograd/ops.rs) -------------
+ * No C entry point in the reference: its GradFn::backward methods compose
+ * ops::* calls on the CPU.  Each function below returns the same tensors
+ * from one fused kernel.  A NULL gradient output is the reference's `None`
+ * (that input does not require grad).  Errors are those of the first
+ * ops::* call that would fail in the reference.  MulScalarBackward
+ * (ops.rs:583-593) is rtc_mul_scalar(grad_output, scalar). */
+
+/* ReluBackward (ops.rs:375-390): grad_output * (input > 0 ? 1 : 0). */
+rtc_result rtc_relu_backward(const rtc_tensor* grad_output, const rtc_tensor* input,
+                             const rtc_tensor* grad_input);
+/* SigmoidBackward (ops.rs:419-431): grad_output * (y * (1 - y)), y the
+ * saved sigmoid output. */
+rtc_result rtc_sigmoid_backward(const rtc_tensor* grad_output, const rtc_tensor* output,
+                                const rtc_tensor* grad_input);
+/* TanhBackward (ops.rs:460-472): grad_output * (1 - y*y), y the saved tanh
+ * output. */
+rtc_result rtc_tanh_backward(const rtc_tensor* grad_output, const rtc_tensor* output,
+                             const rtc_tensor* grad_input);
+/* GeluBackward (ops.rs:3102-3125), from the saved input, with glibc tanhf. */
+rtc_result rtc_gelu_backward(const rtc_tensor* grad_output, const rtc_tensor* input,
+                             const rtc_tensor* grad_input);
+/* autograd's GELU forward (ops.rs:3131-3141), which rounds its cubic term as
+ * ((0.044715*x)*x)*x, unlike ops::gelu (rtc_gelu). */
+rtc_result rtc_autograd_gelu(const rtc_tensor* input, const rtc_tensor* output);
+/* AddBackward (ops.rs:133-149): both gradients are grad_output. */
+rtc_result rtc_add_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
+                            const rtc_tensor* grad_b);
+/* SubBackward (ops.rs:175-192): grad_a = grad_output, grad_b = -grad_output. */
+rtc_result rtc_sub_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
+                            const rtc_tensor* grad_b);
+/* MulBackward (ops.rs:219-236): grad_a = grad_output * b,
+ * grad_b = grad_output * a; one pass when both are wanted. */
+rtc_result rtc_mul_backward(const rtc_tensor* grad_output, const rtc_tensor* a,
+                            const rtc_tensor* b, const rtc_tensor* grad_a,
+                            const rtc_tensor* grad_b);
+/* DivBackward (ops.rs:267-290): grad_a = grad_output / b,
+ * grad_b = grad_output * ((-a) / (b*b)). */
+rtc_result rtc_div_backward(const rtc_tensor* grad_output, const rtc_tensor* a,
+                            const rtc_tensor* b, const rtc_tensor* grad_a,
+                            const rtc_tensor* grad_b);
+/* SumBackward (ops.rs:501-511): grad_input filled with the one element of
+ * grad_output (item(): any other element count is RTC_INVALID_ARGUMENT).
+ * Device tensors only; the value is read on the device. */
+rtc_result rtc_sum_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_input);
+/* MeanBackward (ops.rs:542-552): filled with (f32)((f64)g / n), n =
+ * grad_input's element count.  Device tensors only. */
+rtc_result rtc_mean_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_input);
+/* BroadcastAddBackward (ops.rs:615-693): grad_output folded back onto each
+ * operand's original shape (given by grad_a / grad_b) by reduce_to_shape
+ * (:627-681), in its order: 2-D [1,C] column sums and [R,1] row sums, a copy
+ * for equal element counts, else result[i % m] += grad[i].  Device only. */
+rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
+                                      const rtc_tensor* grad_b);
+
 /* ------------------------------------- flat float32 API (device pointers) */
 /* rusttorch_relu_f32 / add_f32 / mul_f32, ffi/ops.rs:348-389: contiguous f32
  * buffers of `size` elements on the current device. */

@@ -594,6 +594,166 @@ void rto_nn_sgd_step(const float* p, const float* g, const float* vel, size_t n,
 }
 
 /* ------------------------------------------------------------------------ */
+/* autograd backward (core/src/autograd/ops.rs)                             */
+/* ------------------------------------------------------------------------ */
+
+/* :380-387: mask = x > 0 ? 1 : 0, then ops::mul(grad_output, mask) */
+void rto_relu_backward(const float* g, const float* x, float* out, size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    float mask = x[i] > 0.0f ? 1.0f : 0.0f;
+    out[i] = g[i] * mask;
+  }
+}
+
+/* :424-427: one_minus = sub(ones, y); sig_grad = mul(y, one_minus);
+ * grad = mul(grad_output, sig_grad) */
+void rto_sigmoid_backward(const float* g, const float* y, float* out, size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    float one_minus = 1.0f - y[i];
+    float sig_grad = y[i] * one_minus;
+    out[i] = g[i] * sig_grad;
+  }
+}
+
+/* :465-468: sq = mul(y, y); one_minus = sub(ones, sq); grad = mul(g, one_minus) */
+void rto_tanh_backward(const float* g, const float* y, float* out, size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    float sq = y[i] * y[i];
+    float one_minus = 1.0f - sq;
+    out[i] = g[i] * one_minus;
+  }
+}
+
+static float sqrt_2_over_pi(void) {
+  volatile float two = 2.0f, pi = 3.14159265358979323846f;
+  return sqrtf(two / pi);
+}
+
+/* :3108-3118, each Rust f32 expression left to right */
+void rto_gelu_backward(const float* g, const float* x, float* out, size_t n) {
+  const float k = sqrt_2_over_pi();
+  volatile float three = 3.0f, c = 0.044715f;
+  const float c3 = three * c; /* `3.0 * 0.044715` in f32 */
+  for (size_t i = 0; i < n; i++) {
+    float xi = x[i];
+    float x3 = xi * xi;
+    x3 = x3 * xi;
+    float t0 = 0.044715f * x3;
+    t0 = xi + t0;
+    float inner = k * t0;
+    float t = tanhf(inner);
+    float tt = t * t;
+    float sech2 = 1.0f - tt;
+    float d = c3 * xi;
+    d = d * xi;
+    d = 1.0f + d;
+    float d_inner = k * d;
+    float a = 1.0f + t;
+    a = 0.5f * a;
+    float b = 0.5f * xi;
+    b = b * sech2;
+    b = b * d_inner;
+    float s = a + b;
+    out[i] = g[i] * s;
+  }
+}
+
+/* :3136-3141: 0.5 * x * (1.0 + (k * (x + 0.044715 * x * x * x)).tanh()) */
+void rto_autograd_gelu(const float* x, float* out, size_t n) {
+  const float k = sqrt_2_over_pi();
+  for (size_t i = 0; i < n; i++) {
+    float xi = x[i];
+    float c = 0.044715f * xi;
+    c = c * xi;
+    c = c * xi;
+    float inner = xi + c;
+    inner = k * inner;
+    float t = tanhf(inner);
+    float h = 0.5f * xi;
+    float one_t = 1.0f + t;
+    out[i] = h * one_t;
+  }
+}
+
+/* :179-188: grad_output.clone() and grad_output.neg() (a sign flip) */
+void rto_sub_backward(const float* g, float* ga, float* gb, size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    if (ga) ga[i] = g[i];
+    if (gb) gb[i] = -g[i];
+  }
+}
+
+/* :222-231: mul(g, b) and mul(g, a) */
+void rto_mul_backward(const float* g, const float* a, const float* b, float* ga, float* gb,
+                      size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    if (ga) ga[i] = g[i] * b[i];
+    if (gb) gb[i] = g[i] * a[i];
+  }
+}
+
+/* :271-289: div(g, b); b_sq = mul(b, b); neg_a = a.neg();
+ * q = div(neg_a, b_sq); mul(g, q) */
+void rto_div_backward(const float* g, const float* a, const float* b, float* ga, float* gb,
+                      size_t n) {
+  for (size_t i = 0; i < n; i++) {
+    if (ga) ga[i] = g[i] / b[i];
+    if (gb) {
+      float b_sq = b[i] * b[i];
+      float neg_a = -a[i];
+      float q = neg_a / b_sq;
+      gb[i] = g[i] * q;
+    }
+  }
+}
+
+void rto_fill_backward(float g, float* out, size_t n, int mean) {
+  const float v = mean ? (float)((double)g / (double)n) : (float)(double)g;
+  for (size_t i = 0; i < n; i++) out[i] = v;
+}
+
+static size_t numel_of(const size_t* s, size_t nd) {
+  size_t t = 1;
+  for (size_t i = 0; i < nd; i++) t *= s[i];
+  return t;
+}
+
+/* reduce_to_shape, :627-681, branch for branch */
+int rto_reduce_to_shape(const float* grad, const size_t* gshape, size_t gnd, float* out,
+                        const size_t* oshape, size_t ond) {
+  const size_t len = numel_of(gshape, gnd), m = numel_of(oshape, ond);
+  int same = gnd == ond;
+  for (size_t i = 0; same && i < gnd; i++) same = gshape[i] == oshape[i];
+  if (same) {
+    memcpy(out, grad, len * sizeof(float));
+    return RTO_OK;
+  }
+  if (gnd == 2 && ond == 2) {
+    const size_t R = gshape[0], C = gshape[1];
+    if (oshape[0] == 1 && oshape[1] == C) {
+      for (size_t c = 0; c < C; c++) out[c] = 0.0f;
+      for (size_t r = 0; r < R; r++)
+        for (size_t c = 0; c < C; c++) out[c] += grad[r * C + c];
+      return RTO_OK;
+    }
+    if (oshape[1] == 1 && oshape[0] == R) {
+      for (size_t r = 0; r < R; r++) out[r] = 0.0f;
+      for (size_t r = 0; r < R; r++)
+        for (size_t c = 0; c < C; c++) out[r] += grad[r * C + c];
+      return RTO_OK;
+    }
+  }
+  if (len == m) {
+    memcpy(out, grad, len * sizeof(float));
+    return RTO_OK;
+  }
+  if (m == 0) return RTO_INVALID_ARGUMENT;
+  for (size_t j = 0; j < m; j++) out[j] = 0.0f;
+  for (size_t i = 0; i < len; i++) out[i % m] += grad[i];
+  return RTO_OK;
+}
+
+/* ------------------------------------------------------------------------ */
 /* broadcasting (core/src/ops/broadcast.rs)                                 */
 /* ------------------------------------------------------------------------ */
 

@@ -109,6 +109,26 @@ void rto_nn_sgd_step(const float* p, const float* g, const float* vel, size_t n,
 int rto_broadcast_binary(int op, const float* a, const size_t* ashape, size_t andim,
                          const float* b, const size_t* bshape, size_t bndim, float* out);
 
+/* ---- autograd backward: core/src/autograd/ops.rs GradFn::backward ----
+ * Each restates the ops::* chain the reference's backward builds, one f32
+ * rounding per op, in its order.  NULL ga/gb skip that gradient. */
+void rto_relu_backward(const float* g, const float* x, float* out, size_t n);    /* :375-390 */
+void rto_sigmoid_backward(const float* g, const float* y, float* out, size_t n); /* :419-431 */
+void rto_tanh_backward(const float* g, const float* y, float* out, size_t n);    /* :460-472 */
+void rto_gelu_backward(const float* g, const float* x, float* out, size_t n);    /* :3102-3125 */
+void rto_autograd_gelu(const float* x, float* out, size_t n);                    /* :3131-3141 */
+void rto_sub_backward(const float* g, float* ga, float* gb, size_t n);           /* :175-192 */
+void rto_mul_backward(const float* g, const float* a, const float* b, float* ga, float* gb,
+                      size_t n);                                                 /* :219-236 */
+void rto_div_backward(const float* g, const float* a, const float* b, float* ga, float* gb,
+                      size_t n);                                                 /* :267-290 */
+/* SumBackward / MeanBackward (:501-552): Tensor::full(shape, v) with
+ * v = (f32)(f64)g or (f32)((f64)g / n). */
+void rto_fill_backward(float g, float* out, size_t n, int mean);
+/* reduce_to_shape (:627-681): grad of shape gshape folded onto oshape. */
+int rto_reduce_to_shape(const float* grad, const size_t* gshape, size_t gnd, float* out,
+                        const size_t* oshape, size_t ond);
+
 /* ---- seeded synthetic inputs (the generator the tests and the CPU baseline
  * use; the CUDA library carries an identical device generator).  Element i of
  * a stream depends only on (seed, i), so any slice can be regenerated alone.

@@ -309,3 +309,89 @@ def nn_sgd_step(params, grads, velocity, lr, momentum=0.0, weight_decay=0.0):
     check(lib().rtc_nn_sgd_step(params.desc, grads.desc, None, float(lr), float(momentum),
                                 float(weight_decay), po.desc, None))
     return po, None
+
+
+# ---- autograd backward (core autograd/ops.rs GradFn::backward) -------------
+# Each returns what the reference's backward returns for that input; pass
+# need_a / need_b False where the reference's operand does not require grad
+# (its `None`).
+def relu_backward(grad_output: Tensor, input: Tensor) -> Tensor:
+    out = _like(grad_output)
+    check(lib().rtc_relu_backward(grad_output.desc, input.desc, out.desc))
+    return out
+
+
+def sigmoid_backward(grad_output: Tensor, output: Tensor) -> Tensor:
+    out = _like(grad_output)
+    check(lib().rtc_sigmoid_backward(grad_output.desc, output.desc, out.desc))
+    return out
+
+
+def tanh_backward(grad_output: Tensor, output: Tensor) -> Tensor:
+    out = _like(grad_output)
+    check(lib().rtc_tanh_backward(grad_output.desc, output.desc, out.desc))
+    return out
+
+
+def gelu_backward(grad_output: Tensor, input: Tensor) -> Tensor:
+    out = _like(input)
+    check(lib().rtc_gelu_backward(grad_output.desc, input.desc, out.desc))
+    return out
+
+
+def autograd_gelu(x: Tensor) -> Tensor:
+    """autograd's own GELU forward (it rounds differently from gelu)."""
+    out = _like(x)
+    check(lib().rtc_autograd_gelu(x.desc, out.desc))
+    return out
+
+
+def _pair_out(g: Tensor, need_a: bool, need_b: bool):
+    return (_like(g) if need_a else None), (_like(g) if need_b else None)
+
+
+def _d(t):
+    return t.desc if t is not None else None
+
+
+def add_backward(grad_output: Tensor, need_a=True, need_b=True):
+    ga, gb = _pair_out(grad_output, need_a, need_b)
+    check(lib().rtc_add_backward(grad_output.desc, _d(ga), _d(gb)))
+    return ga, gb
+
+
+def sub_backward(grad_output: Tensor, need_a=True, need_b=True):
+    ga, gb = _pair_out(grad_output, need_a, need_b)
+    check(lib().rtc_sub_backward(grad_output.desc, _d(ga), _d(gb)))
+    return ga, gb
+
+
+def mul_backward(grad_output: Tensor, a: Tensor, b: Tensor, need_a=True, need_b=True):
+    ga, gb = _pair_out(grad_output, need_a, need_b)
+    check(lib().rtc_mul_backward(grad_output.desc, a.desc, b.desc, _d(ga), _d(gb)))
+    return ga, gb
+
+
+def div_backward(grad_output: Tensor, a: Tensor, b: Tensor, need_a=True, need_b=True):
+    ga, gb = _pair_out(grad_output, need_a, need_b)
+    check(lib().rtc_div_backward(grad_output.desc, a.desc, b.desc, _d(ga), _d(gb)))
+    return ga, gb
+
+
+def sum_backward(grad_output: Tensor, input_shape) -> Tensor:
+    out = Tensor(list(input_shape), device=grad_output.device)
+    check(lib().rtc_sum_backward(grad_output.desc, out.desc))
+    return out
+
+
+def mean_backward(grad_output: Tensor, input_shape) -> Tensor:
+    out = Tensor(list(input_shape), device=grad_output.device)
+    check(lib().rtc_mean_backward(grad_output.desc, out.desc))
+    return out
+
+
+def broadcast_add_backward(grad_output: Tensor, a_shape, b_shape, need_a=True, need_b=True):
+    ga = Tensor(list(a_shape), device=grad_output.device) if need_a else None
+    gb = Tensor(list(b_shape), device=grad_output.device) if need_b else None
+    check(lib().rtc_broadcast_add_backward(grad_output.desc, _d(ga), _d(gb)))
+    return ga, gb

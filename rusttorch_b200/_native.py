@@ -129,6 +129,18 @@ _SIGNATURES = {
     "rtc_nn_adam_step": (RtcResult, [T, T, T, T, c_float, c_float, c_float, c_float, c_uint64,
                                      T, T, T]),
     "rtc_nn_sgd_step": (RtcResult, [T, T, T, c_float, c_float, c_float, T, T]),
+    "rtc_relu_backward": (RtcResult, [T, T, T]),
+    "rtc_sigmoid_backward": (RtcResult, [T, T, T]),
+    "rtc_tanh_backward": (RtcResult, [T, T, T]),
+    "rtc_gelu_backward": (RtcResult, [T, T, T]),
+    "rtc_autograd_gelu": (RtcResult, [T, T]),
+    "rtc_add_backward": (RtcResult, [T, T, T]),
+    "rtc_sub_backward": (RtcResult, [T, T, T]),
+    "rtc_mul_backward": (RtcResult, [T, T, T, T, T]),
+    "rtc_div_backward": (RtcResult, [T, T, T, T, T]),
+    "rtc_sum_backward": (RtcResult, [T, T]),
+    "rtc_mean_backward": (RtcResult, [T, T]),
+    "rtc_broadcast_add_backward": (RtcResult, [T, T, T]),
     "rtc_relu_f32": (RtcResult, [c_void_p, c_void_p, c_size_t]),
     "rtc_add_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),
     "rtc_mul_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),

@@ -11,6 +11,7 @@
 // cache hint (.cs): every byte is touched once.  Pointers that are not all
 // 16-byte aligned take a scalar grid-stride kernel instead (same results).
 #include "rt_internal.h"
+#include "rt_map.cuh"
 #include "rt_ops.cuh"
 
 #include <algorithm>
@@ -34,119 +35,12 @@ int sm_count(int device) {
   return cache[device];
 }
 
-namespace {
-
-__device__ __forceinline__ float4 ld4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ void st4(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
-
-template <class F>
-__device__ __forceinline__ float4 map4(const F& f, float4 a) {
-  return make_float4(f(a.x), f(a.y), f(a.z), f(a.w));
-}
-template <class F>
-__device__ __forceinline__ float4 map4(const F& f, float4 a, float4 b) {
-  return make_float4(f(a.x, b.x), f(a.y, b.y), f(a.z, b.z), f(a.w, b.w));
-}
-template <class F>
-__device__ __forceinline__ float4 map4(const F& f, float4 a, float4 b, float4 c) {
-  return make_float4(f(a.x, b.x, c.x), f(a.y, b.y, c.y), f(a.z, b.z, c.z), f(a.w, b.w, c.w));
-}
-
-template <int NIN>
-struct In {
-  const float* p[NIN];
-};
-
-template <class F, int NIN>
-__device__ __forceinline__ float apply1(const F& f, const In<NIN>& in, size_t i) {
-  if constexpr (NIN == 1) return f(in.p[0][i]);
-  else if constexpr (NIN == 2) return f(in.p[0][i], in.p[1][i]);
-  else return f(in.p[0][i], in.p[1][i], in.p[2][i]);
-}
-
-// Vectorised map: out[i] = f(in0[i], ...).  The block's tile is U vectors per
-// thread, strided by blockDim so each load instruction is fully coalesced.
-template <class F, int NIN, int U>
-__global__ void __launch_bounds__(kThreads) map_vec_kernel(In<NIN> in, float* out, size_t n, F f) {
-  const size_t n4 = n >> 2;
-  const size_t tile = (size_t)kThreads * U;
-  for (size_t base = (size_t)blockIdx.x * tile + threadIdx.x; base < n4;
-       base += (size_t)gridDim.x * tile) {
-    float4 v[NIN][U];
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-      const size_t j = base + (size_t)u * kThreads;
-      if (j < n4) {
-#pragma unroll
-        for (int k = 0; k < NIN; k++) v[k][u] = ld4(in.p[k] + 4 * j);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-      const size_t j = base + (size_t)u * kThreads;
-      if (j < n4) {
-        float4 r;
-        if constexpr (NIN == 1) r = map4(f, v[0][u]);
-        else if constexpr (NIN == 2) r = map4(f, v[0][u], v[1][u]);
-        else r = map4(f, v[0][u], v[1][u], v[2][u]);
-        st4(out + 4 * j, r);
-      }
-    }
-  }
-  // n % 4 tail elements
-  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
-    const size_t i = (n4 << 2) + threadIdx.x;
-    out[i] = apply1<F, NIN>(f, in, i);
-  }
-}
-
-template <class F, int NIN>
-__global__ void __launch_bounds__(kThreads) map_scalar_kernel(In<NIN> in, float* out, size_t n, F f) {
-  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * kThreads)
-    out[i] = apply1<F, NIN>(f, in, i);
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-int current_device() {
-  int d = 0;
-  cudaGetDevice(&d);
-  return d;
-}
-
-// Grid for a streaming kernel: enough tiles to cover n, capped at a few
-// resident waves (the kernel grid-strides beyond that).
-unsigned grid_for(size_t units, size_t per_block) {
-  const size_t want = (units + per_block - 1) / per_block;
-  const size_t cap = (size_t)sm_count(current_device()) * 8 * 4;
-  return (unsigned)std::max<size_t>(1, std::min(want, cap));
-}
-
-template <class F, int NIN>
-cudaError_t launch_map(const F& f, const In<NIN>& in, float* out, size_t n, cudaStream_t s) {
-  if (n == 0) return cudaSuccess;
-  bool vec = aligned16(out);
-  for (int k = 0; k < NIN; k++) vec = vec && aligned16(in.p[k]);
-  if (vec) {
-    constexpr int U = NIN == 1 ? 4 : (NIN == 2 ? 4 : 2);
-    const unsigned grid = grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * U);
-    map_vec_kernel<F, NIN, U><<<grid, kThreads, 0, s>>>(in, out, n, f);
-  } else {
-    const unsigned grid = grid_for(n, kThreads);
-    map_scalar_kernel<F, NIN><<<grid, kThreads, 0, s>>>(in, out, n, f);
-  }
-  return cudaGetLastError();
-}
-
 // sqrt_2_over_pi = (2.0_f32 / PI).sqrt() (activation.rs:73): f32 division and
 // square root, each correctly rounded.
 float gelu_k() {
   volatile float two = 2.0f, pi = 3.14159265358979323846f;
   return sqrtf(two / pi);
 }
-
-}  // namespace
 
 cudaError_t launch_unary(UnaryOp op, float param, const float* x, float* out, size_t n,
                          cudaStream_t s) {

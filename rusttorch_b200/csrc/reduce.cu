@@ -494,6 +494,76 @@ lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, in
   }
 }
 
+// ------------------------------------------------ last-axis sum, one chain
+// Each lane summed as ONE sequential f32 chain from 0.0, x[0] + x[1] + ...
+// in order (autograd's reduce_to_shape row sums, autograd/ops.rs:650-656).
+// A CTA owns kLcRows lanes whose columns stream through a cp.async ring
+// kLcCols at a time; thread r of the first warp runs lane r's chain out of
+// shared memory.  Rows are padded to 68 floats so the chain threads' 16-byte
+// reads hit distinct banks.  Needs len % 4 == 0 and a 16-byte-aligned base.
+constexpr int kLcRows = 16;
+constexpr int kLcCols = 64;
+constexpr int kLcPitch = kLcCols + 4;
+constexpr int kLcStages = 6;       // 26 KB: 8 CTAs (128 chains) per SM
+constexpr int kLcThreads = 64;
+constexpr int kLcSlots = kLcRows * (kLcCols / 4) / kLcThreads;   // 4 chunks per thread
+
+__global__ void __launch_bounds__(kLcThreads)
+lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
+  __shared__ __align__(16) float smem[kLcStages][kLcRows][kLcPitch];
+  const size_t lane0 = (size_t)blockIdx.x * kLcRows;
+  const int rows = (int)min((size_t)kLcRows, lanes - lane0);
+  const size_t nstage = (len + kLcCols - 1) / kLcCols;
+  const int tid = threadIdx.x;
+  int slot_r[kLcSlots], slot_c[kLcSlots];
+#pragma unroll
+  for (int q = 0; q < kLcSlots; q++) {
+    const int t = tid + q * kLcThreads;
+    slot_r[q] = t / (kLcCols / 4);
+    slot_c[q] = 4 * (t % (kLcCols / 4));
+  }
+  auto issue = [&](size_t st) {
+    if (st < nstage) {
+      const size_t col0 = st * kLcCols;
+      const int cw = (int)min((size_t)kLcCols, len - col0);
+#pragma unroll
+      for (int q = 0; q < kLcSlots; q++)
+        if (slot_r[q] < rows && slot_c[q] < cw)
+          cp_async16(&smem[st % kLcStages][slot_r[q]][slot_c[q]],
+                     x + (lane0 + slot_r[q]) * len + col0 + slot_c[q]);
+    }
+    cp_async_commit();
+  };
+  for (int st = 0; st < kLcStages - 1; st++) issue(st);
+
+  const bool chain = tid < rows;
+  float acc = 0.0f;
+  for (size_t st = 0; st < nstage; st++) {
+    cp_async_wait<kLcStages - 2>();
+    __syncthreads();
+    issue(st + kLcStages - 1);
+    if (chain) {
+      const int n4 = (int)min((size_t)kLcCols, len - st * kLcCols) / 4;
+      const float4* row = reinterpret_cast<const float4*>(&smem[st % kLcStages][tid][0]);
+      int c = 0;
+      for (; c + 4 <= n4; c += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = row[c + u];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          acc = fadd(fadd(fadd(fadd(acc, v[u].x), v[u].y), v[u].z), v[u].w);
+      }
+      for (; c < n4; c++) {
+        const float4 v = row[c];
+        acc = fadd(fadd(fadd(fadd(acc, v.x), v.y), v.z), v.w);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (chain) out[lane0 + tid] = acc;
+}
+
 // Any layout: one thread per output, sequential over len (row order).
 template <int OP>
 __global__ void __launch_bounds__(kThreads)
@@ -618,6 +688,25 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     case kDimMean: lane_generic_kernel<kDimMean><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out); break;
     case kDimMax: lane_generic_kernel<kDimMax><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out); break;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lane_chain_sum(const float* x, size_t lanes, size_t len, float* out,
+                                  cudaStream_t s) {
+  if (lanes == 0) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0) {
+    const size_t grid = (lanes + kLcRows - 1) / kLcRows;
+    for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+      const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+      lane_chain_sum_kernel<<<(unsigned)ng, kLcThreads, 0, s>>>(
+          x + g0 * kLcRows * len, lanes - g0 * kLcRows, len, out + g0 * kLcRows);
+    }
+    return cudaGetLastError();
+  }
+  // lane_generic_kernel<kDimSum> is the same chain, one thread per lane
+  const unsigned grid = (unsigned)std::max<size_t>(
+      1, std::min<size_t>((lanes + kThreads - 1) / kThreads, (size_t)sm_count(cur_device()) * 8));
+  lane_generic_kernel<kDimSum><<<grid, kThreads, 0, s>>>(x, lanes, len, 1, out);
   return cudaGetLastError();
 }
 

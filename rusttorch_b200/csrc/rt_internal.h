@@ -104,6 +104,30 @@ enum DimReduce { kDimSum, kDimMean, kDimMax };
 cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
                               size_t inner, float* out, cudaStream_t s);
 
+// ------------------------------------------------------- autograd backward
+enum GradUnaryOp { kGradRelu, kGradSigmoid, kGradTanh, kGradGelu };
+enum GradBinaryOp { kGradAdd, kGradSub, kGradMul, kGradDiv };
+// out = dL/dx from grad_output g and the saved input (relu, gelu) or output
+// (sigmoid, tanh).
+cudaError_t launch_grad_unary(GradUnaryOp op, const float* g, const float* saved, float* out,
+                              size_t n, cudaStream_t s);
+// grad_a / grad_b may be null (that operand needs no gradient); a and b are
+// read only by mul and div.
+cudaError_t launch_grad_binary(GradBinaryOp op, const float* g, const float* a, const float* b,
+                               float* grad_a, float* grad_b, size_t n, cudaStream_t s);
+// autograd's own gelu forward (autograd/ops.rs:3131), which rounds
+// differently from ops::gelu.
+cudaError_t launch_gelu_autograd(const float* x, float* out, size_t n, cudaStream_t s);
+// out[0..n) = (f32)(f64)g[0], or (f32)((f64)g[0] / divisor) when `divide`.
+cudaError_t launch_fill_from(const float* g, float* out, size_t n, double divisor, bool divide,
+                             cudaStream_t s);
+// Each contiguous lane of length len summed as one sequential f32 chain from
+// 0.0, in element order.
+cudaError_t launch_lane_chain_sum(const float* x, size_t lanes, size_t len, float* out,
+                                  cudaStream_t s);
+// sqrt(2/pi) as the reference computes it in f32.
+float gelu_k();
+
 // -------------------------------------------------------------------- softmax
 cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
                            cudaStream_t s);

@@ -55,6 +55,16 @@ def lib():
                                         c_float, c_uint64, F, F, F]),
             "rto_nn_sgd_step": (None, [F, F, F, c_size_t, c_float, c_float, c_float, F, F]),
             "rto_broadcast_binary": (c_int, [c_int, F, sz, c_size_t, F, sz, c_size_t, F]),
+            "rto_relu_backward": (None, [F, F, F, c_size_t]),
+            "rto_sigmoid_backward": (None, [F, F, F, c_size_t]),
+            "rto_tanh_backward": (None, [F, F, F, c_size_t]),
+            "rto_gelu_backward": (None, [F, F, F, c_size_t]),
+            "rto_autograd_gelu": (None, [F, F, c_size_t]),
+            "rto_sub_backward": (None, [F, F, F, c_size_t]),
+            "rto_mul_backward": (None, [F, F, F, F, F, c_size_t]),
+            "rto_div_backward": (None, [F, F, F, F, F, c_size_t]),
+            "rto_fill_backward": (None, [c_float, F, c_size_t, c_int]),
+            "rto_reduce_to_shape": (c_int, [F, sz, c_size_t, F, sz, c_size_t]),
         }
         for k, (r, a) in sig.items():
             fn = getattr(_lib, k)
@@ -183,3 +193,51 @@ def nn_sgd(pp, g, vel, lr, momentum, wd):
     vel = vel if vel is not None else np.zeros_like(pp)
     lib().rto_nn_sgd_step(p(pp), p(g), p(vel), pp.size, lr, momentum, wd, p(po), p(vo))
     return po, vo
+
+
+# ---- autograd backward (autograd/ops.rs) ----------------------------------
+def grad_unary(name, g, saved):
+    """name in relu, sigmoid, tanh, gelu; saved = input (relu, gelu) or output."""
+    out = np.empty_like(g if name != "gelu" else saved)
+    getattr(lib(), f"rto_{name}_backward")(p(g), p(saved), p(out), saved.size)
+    return out
+
+
+def autograd_gelu(x):
+    out = np.empty_like(x)
+    lib().rto_autograd_gelu(p(x), p(out), x.size)
+    return out
+
+
+def _opt(a):
+    return p(a) if a is not None else None
+
+
+def grad_binary(name, g, a=None, b=None, need_a=True, need_b=True):
+    """name in add, sub, mul, div; returns (grad_a or None, grad_b or None)."""
+    ga = np.empty_like(g) if need_a else None
+    gb = np.empty_like(g) if need_b else None
+    if name == "add":
+        if ga is not None:
+            ga[...] = g
+        if gb is not None:
+            gb[...] = g
+    elif name == "sub":
+        lib().rto_sub_backward(p(g), _opt(ga), _opt(gb), g.size)
+    else:
+        getattr(lib(), f"rto_{name}_backward")(p(g), p(a), p(b), _opt(ga), _opt(gb), g.size)
+    return ga, gb
+
+
+def fill_backward(g, shape, mean):
+    out = np.empty(shape, dtype=np.float32)
+    lib().rto_fill_backward(float(g), p(out), out.size, int(mean))
+    return out
+
+
+def reduce_to_shape(grad, shape):
+    out = np.empty(shape, dtype=np.float32)
+    o = np.empty(1, np.float32) if out.size == 0 else out
+    rc = lib().rto_reduce_to_shape(p(grad), _shape(grad), grad.ndim, p(o),
+                                   (c_size_t * max(1, len(shape)))(*shape), len(shape))
+    return rc, out
