@@ -9,6 +9,7 @@
 // a machine without a GPU.
 #include "../../include/rusttorch_cuda.h"
 #include "rt_abi_util.h"
+#include "rt_tma.cuh"
 #include "rt_internal.h"
 #include "rt_staging.h"
 
@@ -52,6 +53,12 @@ extern "C" void* rtc_get_stream(void) { return static_cast<void*>(thread_stream(
 extern "C" rtc_result rtc_synchronize(void) {
   cudaError_t e = cudaStreamSynchronize(thread_stream());
   if (e != cudaSuccess) return backend_error("cudaStreamSynchronize", e);
+  int device = 0;
+  cudaGetDevice(&device);
+  if (take_wait_timeouts(device))
+    return fail(RTC_BACKEND_ERROR,
+                "a kernel gave up waiting for a shared-memory tile (2 s limit); "
+                "results since the last synchronize are incomplete");
   return ok();
 }
 

@@ -24,6 +24,7 @@
 //    16-byte reads with ~150 KB in flight per SM while every column is still
 //    summed in row order (bit-exact).
 #include "rt_internal.h"
+#include "rt_fold.cuh"
 #include "rt_ops.cuh"
 
 #include <algorithm>
@@ -371,32 +372,15 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
     issue(st + kStages - 1);        // refill the buffer stage st-1 used
     const float* buf = smem + (st % kStages) * stage_floats;
     const int rows = (int)min((size_t)R, len - st * R);
-    if (tid < w_eff) {
-      int r = 0;
-      for (; r + 8 <= rows; r += 8) {
-        float b[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) b[u] = buf[(r + u) * W + tid];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          if (OP == kDimMax) {
-            nan |= b[u] != b[u];
-            acc = fmaxf(acc, b[u]);
-          } else {
-            acc = fadd(acc, b[u]);
-          }
-        }
-      }
-      for (; r < rows; r++) {
-        const float v = buf[r * W + tid];
+    if (tid < w_eff)
+      fold_pipelined(buf + tid, W, rows, [&](float v) {
         if (OP == kDimMax) {
           nan |= v != v;
           acc = fmaxf(acc, v);
         } else {
           acc = fadd(acc, v);
         }
-      }
-    }
+      });
   }
   cp_async_wait<0>();
   if (tid < w_eff) {
@@ -463,16 +447,7 @@ lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, in
     if (chain) {
       const size_t g0 = st * (kLsCols / 8);     // first group of this stage
       const int ng = (int)min((size_t)(kLsCols / 8), steps > g0 ? steps - g0 : 0);
-      const float* row = &smem[st % kLsStages][r][j];
-      int u = 0;
-      for (; u + 8 <= ng; u += 8) {
-        float b[8];
-#pragma unroll
-        for (int w = 0; w < 8; w++) b[w] = row[8 * (u + w)];
-#pragma unroll
-        for (int w = 0; w < 8; w++) p = fadd(p, b[w]);
-      }
-      for (; u < ng; u++) p = fadd(p, row[8 * u]);
+      fold_pipelined(&smem[st % kLsStages][r][j], 8, ng, [&](float v) { p = fadd(p, v); });
     }
   }
   cp_async_wait<0>();
@@ -545,14 +520,19 @@ lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
     if (chain) {
       const int n4 = (int)min((size_t)kLcCols, len - st * kLcCols) / 4;
       const float4* row = reinterpret_cast<const float4*>(&smem[st % kLcStages][tid][0]);
+      // 16-byte reads, two groups of four ahead of the chain
       int c = 0;
-      for (; c + 4 <= n4; c += 4) {
-        float4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) v[u] = row[c + u];
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-          acc = fadd(fadd(fadd(fadd(acc, v[u].x), v[u].y), v[u].z), v[u].w);
+      if (n4 >= 2) {
+        float4 cur0 = row[0], cur1 = row[1];
+        for (c = 2; c + 2 <= n4; c += 2) {
+          const float4 nxt0 = row[c], nxt1 = row[c + 1];
+          acc = fadd(fadd(fadd(fadd(acc, cur0.x), cur0.y), cur0.z), cur0.w);
+          acc = fadd(fadd(fadd(fadd(acc, cur1.x), cur1.y), cur1.z), cur1.w);
+          cur0 = nxt0;
+          cur1 = nxt1;
+        }
+        acc = fadd(fadd(fadd(fadd(acc, cur0.x), cur0.y), cur0.z), cur0.w);
+        acc = fadd(fadd(fadd(fadd(acc, cur1.x), cur1.y), cur1.z), cur1.w);
       }
       for (; c < n4; c++) {
         const float4 v = row[c];
@@ -671,6 +651,11 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
       lane_sum8_kernel<<<grid, kLaneThreads, 0, s>>>(x, lanes, len, out, op == kDimMean);
     }
     return cudaGetLastError();
+  }
+  {
+    bool used = false;
+    const cudaError_t e = launch_strip_tma(op, x, outer, len, inner, out, s, &used);
+    if (e != cudaSuccess || used) return e;
   }
   const bool strip_ok = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && inner % 4 == 0 &&
                         inner >= 32 && len >= 1;

@@ -103,6 +103,10 @@ enum DimReduce { kDimSum, kDimMean, kDimMax };
 // inner == 1 is the contiguous-lane (last axis) case.
 cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
                               size_t inner, float* out, cudaStream_t s);
+// The TMA-staged variant for inner > 1 (strip_tma.cu).  Sets *used = false
+// (and launches nothing) when the layout does not suit TMA.
+cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t len,
+                             size_t inner, float* out, cudaStream_t s, bool* used);
 
 // ------------------------------------------------------- autograd backward
 enum GradUnaryOp { kGradRelu, kGradSigmoid, kGradTanh, kGradGelu };

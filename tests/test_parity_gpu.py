@@ -279,6 +279,23 @@ def test_dim_reduction_shapes(shape, op):
         assert_bits_equal(got, O.reduce_dim(op, x, dim), f"{op}_dim {shape} dim={dim}")
 
 
+@pytest.mark.parametrize("shape,dim", [((32768, 4096), 0), ((4, 1000, 132), 1), ((3, 777, 4), 1),
+                                       ((1000, 2, 8), 1), ((2049, 300), 0), ((5, 3, 4096), 1),
+                                       ((1 << 20, 4), 0), ((257, 1028), 0)])
+@pytest.mark.parametrize("op", ["sum", "mean", "max"])
+def test_tma_strip_shapes(shape, dim, op):
+    """Non-last-axis reductions on the TMA-staged path: ragged last tiles
+    (rows and columns), several outer slices, NaN and zero columns."""
+    x = O.normal(int(np.prod(shape)), 48, 0, 2).reshape(shape)
+    flat = x.reshape(-1, shape[-1])
+    flat[3, 1] = np.nan
+    flat[:, 2] = -np.abs(flat[:, 2])
+    flat[7 % flat.shape[0], 2] = 0.0
+    got = getattr(rt, f"{op}_dim")(dev(x), dim).to_numpy()
+    rt.synchronize()          # raises if a kernel gave up a bounded wait
+    assert_bits_equal(got, O.reduce_dim(op, x, dim), f"{op}_dim {shape} dim={dim}")
+
+
 def test_max_dim_with_nan_and_zero_lanes():
     x = O.normal(6 * 40, 47).reshape(6, 40)
     x[0, 10] = np.nan
