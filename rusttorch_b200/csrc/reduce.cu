@@ -404,10 +404,12 @@ __global__ void strip_reduce_kernel(const float* x, size_t len, size_t inner, in
 constexpr int kLsRows = 4;
 constexpr int kLsCols = 256;
 constexpr int kLsPitch = kLsCols + 8;
-constexpr int kLsStages = 4;      // ~17 KB: 13 CTAs per SM, one wave for 8192 lanes
 constexpr int kLsThreads = 64;
 constexpr int kLsSlots = kLsRows * (kLsCols / 4) / kLsThreads;   // 4 chunks per thread
 
+// kLsStages-deep ring (3 to 6 stages; the launcher picks the deepest whose
+// CTAs all fit on the GPU at once, since each CTA's lanes take equally long).
+template <int kLsStages>
 __global__ void __launch_bounds__(kLsThreads)
 lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
   __shared__ __align__(16) float smem[kLsStages][kLsRows][kLsPitch];
@@ -640,11 +642,29 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
       lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
     } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
       const size_t grid = (lanes + kLsRows - 1) / kLsRows;
+      // deepest ring whose CTAs are all resident in one wave (else 4)
+      const size_t sms = (size_t)sm_count(cur_device());
+      auto slots = [&](int stages) {
+        const size_t smem = (size_t)stages * kLsRows * kLsPitch * sizeof(float) + 1024;
+        return sms * std::min<size_t>((227u << 10) / smem, 2048 / kLsThreads);
+      };
+      int stages = 4;
+      for (int c = 6; c >= 3; c--)
+        if (grid <= slots(c)) {
+          stages = c;
+          break;
+        }
       for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
         const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
-        lane_sum8_staged_kernel<<<(unsigned)ng, kLsThreads, 0, s>>>(
-            x + g0 * kLsRows * len, lanes - g0 * kLsRows, len, out + g0 * kLsRows,
-            op == kDimMean);
+        const float* xs = x + g0 * kLsRows * len;
+        float* os = out + g0 * kLsRows;
+        const size_t nl = lanes - g0 * kLsRows;
+        switch (stages) {
+          case 3: lane_sum8_staged_kernel<3><<<(unsigned)ng, kLsThreads, 0, s>>>(xs, nl, len, os, op == kDimMean); break;
+          case 5: lane_sum8_staged_kernel<5><<<(unsigned)ng, kLsThreads, 0, s>>>(xs, nl, len, os, op == kDimMean); break;
+          case 6: lane_sum8_staged_kernel<6><<<(unsigned)ng, kLsThreads, 0, s>>>(xs, nl, len, os, op == kDimMean); break;
+          default: lane_sum8_staged_kernel<4><<<(unsigned)ng, kLsThreads, 0, s>>>(xs, nl, len, os, op == kDimMean); break;
+        }
       }
     } else {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
