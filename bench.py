@@ -506,6 +506,17 @@ def run_suite(args) -> None:
            lambda: N.check(lib.rtc_mul_scalar(a[1].ref, 0.5, c[1].ref)))
     timeit("add->mul_scalar (fused)", f"cfg1 [{N1}]", 12 * N1,
            lambda: N.check(lib.rtc_add_mul_scalar(a[1].ref, b[1].ref, 0.5, c[1].ref)))
+    # losses (ops/loss.rs) on cfg1's shape: the ordered f32 chains are
+    # serial, so these are bound by n/8 (or n) dependent adds, not by HBM
+    v1 = c_double()
+    fill(c, 102, False, 0.0, 1.0)
+    for name, fn, extra in (("mse_loss", lib.rtc_mse_loss, ()),
+                           ("l1_loss", lib.rtc_l1_loss, ()),
+                           ("smooth_l1_loss", lib.rtc_smooth_l1_loss, (1.0,)),
+                           ("binary_cross_entropy_loss", lib.rtc_binary_cross_entropy_loss, (1e-7,)),
+                           ("cross_entropy_loss", lib.rtc_cross_entropy_loss, (1e-7,))):
+        timeit(name, f"cfg1 [{N1}]", 8 * N1,
+               lambda fn=fn, extra=extra: N.check(fn(c[1].ref, a[1].ref, *extra, byref(v1))))
     del a, b, c
     # cfg2
     x = t([N2])

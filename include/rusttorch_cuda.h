@@ -295,6 +295,34 @@ rtc_result rtc_nn_sgd_step(const rtc_tensor* params, const rtc_tensor* grads,
                            float weight_decay, const rtc_tensor* params_out,
                            const rtc_tensor* velocity_out);
 
+/* ---- loss functions (rusttorch-core src/ops/loss.rs) --------------------
+ * No C entry point in the reference (Rust functions returning Result<f64>).
+ * *out_value = the reference's f64 result: the f32 sum of the per-element
+ * terms, in the reference's order, as f64, divided by the element count.
+ * mse/l1/smooth_l1 sum like ndarray's sum() (eight sequential chains) and
+ * are bit-identical; bce/ce sum one chain from -0.0 like Iterator::sum and
+ * use a correctly rounded logf (glibc's logf differs from it in the last
+ * bit for about 0.02% of inputs).  The chains are serial: their time is
+ * about n/8 (or n) dependent f32 adds on one SM.  Device f32 tensors;
+ * synchronous. */
+
+/* mse_loss (loss.rs:41-85): mean((p - t)^2). */
+rtc_result rtc_mse_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
+                        double* out_value);
+/* l1_loss (loss.rs:102-144): mean(|p - t|). */
+rtc_result rtc_l1_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
+                       double* out_value);
+/* smooth_l1_loss (loss.rs:165-229); beta <= 0 is RTC_INVALID_ARGUMENT. */
+rtc_result rtc_smooth_l1_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
+                              double beta, double* out_value);
+/* binary_cross_entropy_loss (loss.rs:249-315); epsilon must be in (0, 1). */
+rtc_result rtc_binary_cross_entropy_loss(const rtc_tensor* predictions,
+                                         const rtc_tensor* targets, double epsilon,
+                                         double* out_value);
+/* cross_entropy_loss (loss.rs:332-391); epsilon must be in (0, 1). */
+rtc_result rtc_cross_entropy_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
+                                  double epsilon, double* out_value);
+
 /* ---- autograd backward (rusttorch-core src/autograd/ops.rs) -------------
  * No C entry point in the reference: its GradFn::backward methods compose
  * ops::* calls on the CPU.  Each function below returns the same tensors

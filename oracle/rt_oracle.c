@@ -594,6 +594,85 @@ void rto_nn_sgd_step(const float* p, const float* g, const float* vel, size_t n,
 }
 
 /* ------------------------------------------------------------------------ */
+/* loss functions (core/src/ops/loss.rs)                                    */
+/* ------------------------------------------------------------------------ */
+
+/* ndarray's arithmetic allocates each intermediate (diff, squared, ...) and
+ * sum() folds the last one with unrolled_fold; the terms are computed here
+ * into one buffer first, in the same f32 operations. */
+static double terms_mean8(float* terms, size_t n) {
+  const float s = unrolled_sum(terms, n, 1);
+  free(terms);
+  return (double)s / (double)n;
+}
+
+double rto_mse_loss(const float* p, const float* t, size_t n) {
+  float* d = (float*)malloc((n ? n : 1) * sizeof(float));
+  for (size_t i = 0; i < n; i++) {
+    float diff = p[i] - t[i]; /* :72 pred - targ */
+    d[i] = diff * diff;       /* :73 &diff * &diff; :74 sum() */
+  }
+  return terms_mean8(d, n);
+}
+
+double rto_l1_loss(const float* p, const float* t, size_t n) {
+  float* d = (float*)malloc((n ? n : 1) * sizeof(float));
+  for (size_t i = 0; i < n; i++) d[i] = fabsf(p[i] - t[i]); /* :133-134 */
+  return terms_mean8(d, n);
+}
+
+/* :204-213: |x| < beta ? 0.5*x*x/beta : |x| - 0.5*beta, beta as f32 */
+double rto_smooth_l1_loss(const float* p, const float* t, size_t n, double beta) {
+  const float b = (float)beta;
+  float* d = (float*)malloc((n ? n : 1) * sizeof(float));
+  for (size_t i = 0; i < n; i++) {
+    float x = p[i] - t[i];
+    float ax = fabsf(x);
+    if (ax < b) {
+      float h = 0.5f * x;
+      h = h * x;
+      d[i] = h / b;
+    } else {
+      float hb = 0.5f * b;
+      d[i] = ax - hb;
+    }
+  }
+  return terms_mean8(d, n);
+}
+
+/* f32::max / f32::min: the other operand when one is NaN (IEEE maxNum). */
+static float rust_max(float a, float b) { return a != a ? b : (b != b ? a : (a > b ? a : b)); }
+static float rust_min(float a, float b) { return a != a ? b : (b != b ? a : (a < b ? a : b)); }
+
+/* :284-292: the terms folded in order by Iterator::sum::<f32>() (from -0.0) */
+double rto_bce_loss(const float* p, const float* t, size_t n, double epsilon) {
+  const float e = (float)epsilon;
+  const float hi = 1.0f - e;
+  float acc = -0.0f;
+  for (size_t i = 0; i < n; i++) {
+    float pc = rust_min(rust_max(p[i], e), hi);
+    float a = t[i] * logf(pc);
+    float om = 1.0f - t[i];
+    float b = om * logf(1.0f - pc);
+    float s = a + b;
+    acc = acc + (-s);
+  }
+  return (double)acc / (double)n;
+}
+
+/* :363-370: -t * ln(max(p, eps)), folded in order from -0.0 */
+double rto_ce_loss(const float* p, const float* t, size_t n, double epsilon) {
+  const float e = (float)epsilon;
+  float acc = -0.0f;
+  for (size_t i = 0; i < n; i++) {
+    float pc = rust_max(p[i], e);
+    float term = (-t[i]) * logf(pc);
+    acc = acc + term;
+  }
+  return (double)acc / (double)n;
+}
+
+/* ------------------------------------------------------------------------ */
 /* autograd backward (core/src/autograd/ops.rs)                             */
 /* ------------------------------------------------------------------------ */
 

@@ -129,6 +129,17 @@ void rto_fill_backward(float g, float* out, size_t n, int mean);
 int rto_reduce_to_shape(const float* grad, const size_t* gshape, size_t gnd, float* out,
                         const size_t* oshape, size_t ond);
 
+/* ---- loss functions: core/src/ops/loss.rs (f32 inputs) ----
+ * Each returns the reference's f64 result: the f32 sum of the per-element
+ * terms, as f64, divided by n.  mse/l1/smooth_l1 sum with ndarray's sum()
+ * (unrolled_fold: eight chains); bce/ce with Iterator::sum::<f32>() (one
+ * chain from -0.0).  Argument checks are the caller's. */
+double rto_mse_loss(const float* p, const float* t, size_t n);                    /* :41-85 (f32 path :71-75) */
+double rto_l1_loss(const float* p, const float* t, size_t n);                     /* :102-144 (:132-135) */
+double rto_smooth_l1_loss(const float* p, const float* t, size_t n, double beta); /* :165-229 (:203-214) */
+double rto_bce_loss(const float* p, const float* t, size_t n, double epsilon);    /* :249-315 (:283-294) */
+double rto_ce_loss(const float* p, const float* t, size_t n, double epsilon);     /* :332-391 (:362-372) */
+
 /* ---- seeded synthetic inputs (the generator the tests and the CPU baseline
  * use; the CUDA library carries an identical device generator).  Element i of
  * a stream depends only on (seed, i), so any slice can be regenerated alone.

@@ -395,3 +395,30 @@ def broadcast_add_backward(grad_output: Tensor, a_shape, b_shape, need_a=True, n
     gb = Tensor(list(b_shape), device=grad_output.device) if need_b else None
     check(lib().rtc_broadcast_add_backward(grad_output.desc, _d(ga), _d(gb)))
     return ga, gb
+
+
+# ---- loss functions (core ops/loss.rs): Python floats, like rusttorch's f64 --
+def _loss(fn, predictions: Tensor, targets: Tensor, *args) -> float:
+    v = ctypes.c_double()
+    check(fn(predictions.desc, targets.desc, *args, ctypes.byref(v)))
+    return v.value
+
+
+def mse_loss(predictions: Tensor, targets: Tensor) -> float:
+    return _loss(lib().rtc_mse_loss, predictions, targets)
+
+
+def l1_loss(predictions: Tensor, targets: Tensor) -> float:
+    return _loss(lib().rtc_l1_loss, predictions, targets)
+
+
+def smooth_l1_loss(predictions: Tensor, targets: Tensor, beta: float = 1.0) -> float:
+    return _loss(lib().rtc_smooth_l1_loss, predictions, targets, float(beta))
+
+
+def binary_cross_entropy_loss(predictions: Tensor, targets: Tensor, epsilon: float = 1e-7) -> float:
+    return _loss(lib().rtc_binary_cross_entropy_loss, predictions, targets, float(epsilon))
+
+
+def cross_entropy_loss(predictions: Tensor, targets: Tensor, epsilon: float = 1e-7) -> float:
+    return _loss(lib().rtc_cross_entropy_loss, predictions, targets, float(epsilon))

@@ -129,6 +129,11 @@ _SIGNATURES = {
     "rtc_nn_adam_step": (RtcResult, [T, T, T, T, c_float, c_float, c_float, c_float, c_uint64,
                                      T, T, T]),
     "rtc_nn_sgd_step": (RtcResult, [T, T, T, c_float, c_float, c_float, T, T]),
+    "rtc_mse_loss": (RtcResult, [T, T, POINTER(c_double)]),
+    "rtc_l1_loss": (RtcResult, [T, T, POINTER(c_double)]),
+    "rtc_smooth_l1_loss": (RtcResult, [T, T, c_double, POINTER(c_double)]),
+    "rtc_binary_cross_entropy_loss": (RtcResult, [T, T, c_double, POINTER(c_double)]),
+    "rtc_cross_entropy_loss": (RtcResult, [T, T, c_double, POINTER(c_double)]),
     "rtc_relu_backward": (RtcResult, [T, T, T]),
     "rtc_sigmoid_backward": (RtcResult, [T, T, T]),
     "rtc_tanh_backward": (RtcResult, [T, T, T]),

@@ -132,6 +132,14 @@ cudaError_t launch_lane_chain_sum(const float* x, size_t lanes, size_t len, floa
 // sqrt(2/pi) as the reference computes it in f32.
 float gelu_k();
 
+// ------------------------------------------------------------------- losses
+enum LossOp { kLossMse, kLossL1, kLossSmoothL1, kLossBce, kLossCe };
+// *sum_out (device) = the reference's ordered f32 sum of the loss terms of
+// p and t; `terms` is n floats of 16-byte-aligned device scratch.  a, b:
+// smooth_l1 (beta, 0.5*beta), bce (eps, 1 - eps), ce (eps, unused), in f32.
+cudaError_t launch_loss(LossOp op, const float* p, const float* t, size_t n, float a, float b,
+                        float* terms, float* sum_out, cudaStream_t s);
+
 // -------------------------------------------------------------------- softmax
 cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
                            cudaStream_t s);

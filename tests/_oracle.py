@@ -55,6 +55,11 @@ def lib():
                                         c_float, c_uint64, F, F, F]),
             "rto_nn_sgd_step": (None, [F, F, F, c_size_t, c_float, c_float, c_float, F, F]),
             "rto_broadcast_binary": (c_int, [c_int, F, sz, c_size_t, F, sz, c_size_t, F]),
+            "rto_mse_loss": (c_double, [F, F, c_size_t]),
+            "rto_l1_loss": (c_double, [F, F, c_size_t]),
+            "rto_smooth_l1_loss": (c_double, [F, F, c_size_t, c_double]),
+            "rto_bce_loss": (c_double, [F, F, c_size_t, c_double]),
+            "rto_ce_loss": (c_double, [F, F, c_size_t, c_double]),
             "rto_relu_backward": (None, [F, F, F, c_size_t]),
             "rto_sigmoid_backward": (None, [F, F, F, c_size_t]),
             "rto_tanh_backward": (None, [F, F, F, c_size_t]),
@@ -241,3 +246,9 @@ def reduce_to_shape(grad, shape):
     rc = lib().rto_reduce_to_shape(p(grad), _shape(grad), grad.ndim, p(o),
                                    (c_size_t * max(1, len(shape)))(*shape), len(shape))
     return rc, out
+
+
+# ---- losses (ops/loss.rs) -------------------------------------------------
+def loss(name, pred, targ, *param):
+    """name in mse, l1, smooth_l1, bce, ce; returns the reference's f64."""
+    return getattr(lib(), f"rto_{name}_loss")(p(pred), p(targ), pred.size, *map(float, param))
