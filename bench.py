@@ -559,8 +559,9 @@ def run_suite(args) -> None:
     timeit("add_broadcast (row bias)", f"cfg4 [{R4},{C4}] + [{C4}]", 8 * R4 * C4 + 4 * C4,
            lambda: N.check(lib.rtc_add_broadcast(x[1].ref, bias[1].ref, y[1].ref)))
     # autograd backward (autograd/ops.rs) on cfg4's shape
-    g, z = t([R4, C4]), t([R4, C4])
+    g, z, w = t([R4, C4]), t([R4, C4]), t([R4, C4])
     fill(g, 10, True, 0.0, 1.0)
+    fill(z, 11, True, 1.0, 0.5)
     for name in ("relu", "sigmoid", "tanh", "gelu"):
         fn = getattr(lib, f"rtc_{name}_backward")
         timeit(f"{name}_backward", f"cfg4 [{R4},{C4}]", 12 * R4 * C4,
@@ -568,13 +569,13 @@ def run_suite(args) -> None:
     for name in ("mul", "div"):
         fn = getattr(lib, f"rtc_{name}_backward")
         timeit(f"{name}_backward (both grads)", f"cfg4 [{R4},{C4}]", 20 * R4 * C4,
-               lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, g[1].ref, y[1].ref, z[1].ref)))
+               lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, z[1].ref, y[1].ref, w[1].ref)))
     cols, rows = t([1, C4]), t([R4, 1])
     timeit("broadcast_add_backward -> [1,C]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * C4,
            lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, cols[1].ref, None)))
     timeit("broadcast_add_backward -> [R,1]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * R4,
            lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, rows[1].ref, None)))
-    del x, y, g, z
+    del x, y, g, z, w
     # cfg5
     P = {k: t([N5]) for k in "pgmv"}
     fill(P["p"], 51, True, 0.0, 0.02)
