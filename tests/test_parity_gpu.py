@@ -189,6 +189,30 @@ def test_softmax_special_rows():
     assert_bits_equal(rt.softmax(dev(x), 1).to_numpy(), O.softmax(x, 1), "softmax specials")
 
 
+@pytest.mark.parametrize("shape", [(20000, 640), (3000, 2048), (2500, 4096), (1000, 512),
+                                   (999, 1028), (7, 3000)])
+def test_softmax_pipelined_rows(shape):
+    """Many rows at each register tier of the row kernel, with rows of NaN,
+    -inf, +inf, zeros and huge values among ordinary ones."""
+    rows, n = shape
+    x = O.normal(rows * n, 44, 0, 3).reshape(shape)
+    for r in range(0, rows, max(1, rows // 7)):
+        k = (r // max(1, rows // 7)) % 5
+        if k == 0:
+            x[r, r % n] = np.nan
+        elif k == 1:
+            x[r, :] = -np.inf
+        elif k == 2:
+            x[r, (3 * r) % n] = np.inf
+        elif k == 3:
+            x[r, :] = 0.0
+        else:
+            x[r, :] = 1e30
+    got = rt.softmax(dev(x), 1).to_numpy()
+    rt.synchronize()          # raises if a kernel gave up a bounded wait
+    assert_bits_equal(got, O.softmax(x, 1), f"softmax {shape}")
+
+
 # ---------------------------------------------------------------- cfg 2
 def _check_sum(got, x):
     want = O.sum(x)
