@@ -67,28 +67,84 @@ def env_int(k, d):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks during the timed region."""
+    """This GPU's SM clock and clock-event (throttle) reasons, sampled every
+    few milliseconds during the timed region by a thread reading NVML (read
+    only: nothing is set).  Falls back to `nvidia-smi -lms 50` if NVML is
+    unavailable."""
 
+    # nvmlClocksEventReasons bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples = []          # (sm_mhz, max_mhz, reason_bits)
         self.proc = None
+        self.thread = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"rt_clocks_{os.getpid()}.csv"
+
+    def _handle(self, pynvml):
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _sample(self):
+        p = self.nvml
+        sm = p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)
+        try:
+            bits = p.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            bits = p.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        self.samples.append((sm, self.max_mhz, bits))
+
+    def _loop(self):
+        while not self.stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            self.stop.wait(self.period)
 
     def __enter__(self):
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            import threading
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = self._handle(pynvml)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._sample()
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
+            try:
+                self.f = open(self.path, "w")
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-i", str(self.cuda_index), "-lms", "50"], stdout=self.f,
+                    stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._sample()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -98,6 +154,12 @@ class ClockSampler:
             self.f.close()
 
     def summary(self) -> dict:
+        if self.samples:
+            sm = [float(s[0]) for s in self.samples]
+            reasons = sorted({name for _, _, bits in self.samples
+                              for bit, name in self.REASONS.items() if bits & bit})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(self.samples[0][1]),
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
         rows = []
         try:
             for line in self.path.read_text().splitlines():
@@ -114,7 +176,7 @@ class ClockSampler:
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ------------------------------------------------------------- CPU baseline
