@@ -37,28 +37,42 @@ bcast_kernel(const float* a, const float* b, float* out, size_t n, BcastPlan pla
 // Two collapsed dims [M, N]: no division per element.  Rows are strided
 // over blockIdx.y, columns over x; float4 when a's rows are contiguous and b
 // is either a contiguous row or a broadcast scalar per row.
+constexpr int kRowsPerIter = 4;
+
 template <class F, bool VEC>
 __global__ void __launch_bounds__(kThreads)
 bcast2_kernel(const float* a, const float* b, float* out, long long M, long long N,
               long long as0, long long as1, long long bs0, long long bs1, F f) {
   if (VEC) {
+    // kRowsPerIter rows per iteration, all loads issued before any store, so
+    // each thread keeps several 16-byte loads in flight.
     const long long n4 = N / 4;
-    for (long long r = blockIdx.y; r < M; r += gridDim.y) {
-      const float* ar = a + r * as0;
-      const float* br = b + r * bs0;
-      float* orow = out + r * N;
+    for (long long r0 = (long long)blockIdx.y * kRowsPerIter; r0 < M;
+         r0 += (long long)gridDim.y * kRowsPerIter) {
       for (long long c = (long long)blockIdx.x * kThreads + threadIdx.x; c < n4;
            c += (long long)gridDim.x * kThreads) {
-        const float4 x = __ldcs(reinterpret_cast<const float4*>(ar) + c);
-        float4 y;
-        if (bs1 == 0) {
-          const float v = __ldg(br);
-          y = make_float4(v, v, v, v);
-        } else {
-          y = __ldg(reinterpret_cast<const float4*>(br) + c);
+        float4 x[kRowsPerIter], y[kRowsPerIter];
+#pragma unroll
+        for (int k = 0; k < kRowsPerIter; k++) {
+          const long long r = r0 + k;
+          if (r < M) {
+            x[k] = __ldcs(reinterpret_cast<const float4*>(a + r * as0) + c);
+            if (bs1 == 0) {
+              const float v = __ldg(b + r * bs0);
+              y[k] = make_float4(v, v, v, v);
+            } else {
+              y[k] = __ldg(reinterpret_cast<const float4*>(b + r * bs0) + c);
+            }
+          }
         }
-        __stcs(reinterpret_cast<float4*>(orow) + c,
-               make_float4(f(x.x, y.x), f(x.y, y.y), f(x.z, y.z), f(x.w, y.w)));
+#pragma unroll
+        for (int k = 0; k < kRowsPerIter; k++) {
+          const long long r = r0 + k;
+          if (r < M)
+            __stcs(reinterpret_cast<float4*>(out + r * N) + c,
+                   make_float4(f(x[k].x, y[k].x), f(x[k].y, y[k].y), f(x[k].z, y[k].z),
+                               f(x[k].w, y[k].w)));
+        }
       }
     }
   } else {
@@ -87,7 +101,9 @@ cudaError_t launch(const F& f, const float* a, const float* b, float* out, size_
     const unsigned gx = (unsigned)std::max<long long>(
         1, std::min<long long>((cols + kThreads - 1) / kThreads, 64));
     const long long want_y = (long long)sm_count(dev) * 16 / gx + 1;
-    const unsigned gy = (unsigned)std::max<long long>(1, std::min<long long>(M, std::min<long long>(want_y, 65535)));
+    const long long row_groups = vec ? (M + kRowsPerIter - 1) / kRowsPerIter : M;
+    const unsigned gy = (unsigned)std::max<long long>(
+        1, std::min<long long>(row_groups, std::min<long long>(want_y, 65535)));
     if (vec) {
       // A row-broadcast b (bs1 == 1, bs0 == 0) or column-broadcast b (bs1 == 0).
       bcast2_kernel<F, true><<<dim3(gx, gy), kThreads, 0, s>>>(a, b, out, M, N, as0, as1, bs0,

@@ -270,10 +270,28 @@ void release_library_state() {
 
 // ------------------------------------------------------ exact global stats
 
-static cudaError_t read_elem(const float* x, size_t i, cudaStream_t s, float* v) {
-  cudaError_t e = cudaMemcpyAsync(v, x + i, sizeof(float), cudaMemcpyDeviceToHost, s);
+// A small page-locked buffer per host thread for the scalars these paths
+// return: a device-to-host copy into pinned memory is one DMA, where pageable
+// memory goes through the driver's staging buffer.  Allocated on first use
+// and kept for the thread's life (256 bytes).
+static void* pinned_scratch() {
+  static thread_local void* p = nullptr;
+  if (!p && cudaHostAlloc(&p, 256, cudaHostAllocPortable) != cudaSuccess) p = nullptr;
+  return p;
+}
+
+// Copies `bytes` (<= 256) from the device to *dst through the pinned buffer
+// (or directly when it is unavailable) and waits for them.
+static cudaError_t fetch(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  void* pin = pinned_scratch();
+  cudaError_t e = cudaMemcpyAsync(pin ? pin : dst, src, bytes, cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && pin) std::memcpy(dst, pin, bytes);
   return e;
+}
+
+static cudaError_t read_elem(const float* x, size_t i, cudaStream_t s, float* v) {
+  return fetch(v, x + i, sizeof(float), s);
 }
 
 #define CK(call)                         \
@@ -300,8 +318,7 @@ cudaError_t exact_global_stats(const float* x, size_t n, int device, int want, c
 
   CK(launch_stats(x, n, parts, nparts, res, s));
   StatsPart h;
-  CK(cudaMemcpyAsync(&h, res, sizeof h, cudaMemcpyDeviceToHost, s));
-  CK(cudaStreamSynchronize(s));
+  CK(fetch(&h, res, sizeof h, s));
   out->sum = h.sum;
   out->max = h.mx;
   out->min = h.mn;
@@ -315,8 +332,7 @@ cudaError_t exact_global_stats(const float* x, size_t n, int device, int want, c
   if (fix_max || fix_min) {
     IndexScan hs;
     CK(launch_index_scan(x, n, scan, s));
-    CK(cudaMemcpyAsync(&hs, scan, sizeof hs, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
+    CK(fetch(&hs, scan, sizeof hs, s));
     if (fix_max) {
       // The fold restarts after the last NaN; if x[n-1] is NaN it ends there.
       if (hs.last_nan == n) {
@@ -329,8 +345,7 @@ cudaError_t exact_global_stats(const float* x, size_t n, int device, int want, c
           const int np2 = stats_num_parts(device, n - start);
           CK(launch_stats(x + start, n - start, parts, np2, res, s));
           StatsPart h2;
-          CK(cudaMemcpyAsync(&h2, res, sizeof h2, cudaMemcpyDeviceToHost, s));
-          CK(cudaStreamSynchronize(s));
+          CK(fetch(&h2, res, sizeof h2, s));
           m = h2.mx;
           out->max_const = true;
         }
