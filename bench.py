@@ -46,8 +46,10 @@ BYTES = {
     "softmax": 8 * R4 * C4,
     "adamw": 28 * N5,
 }
+ELEMS = {"add_mul_scalar": N1, "sum": N2, "softmax": R4 * C4, "adamw": N5}
 OPS = list(BYTES)
 FALLBACK_HBM_GBS = 6650.0
+SPEC_HBM_GBS = 8000.0              # B200 HBM3e data-sheet figure, for context
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -402,7 +404,9 @@ def main() -> None:
     value = step_bytes / (ms_step * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
     per_op = {o: {"ms": op_ms[o], "GB_s": BYTES[o] / (op_ms[o] * 1e-3) / 1e9,
-                  "frac_of_measured_peak": BYTES[o] / (op_ms[o] * 1e-3) / 1e9 / peak}
+                  "elements_per_s": ELEMS[o] / (op_ms[o] * 1e-3),
+                  "frac_of_measured_peak": BYTES[o] / (op_ms[o] * 1e-3) / 1e9 / peak,
+                  "frac_of_8TBs_spec": BYTES[o] / (op_ms[o] * 1e-3) / 1e9 / SPEC_HBM_GBS}
               for o in ops}
     dom = max(ops, key=lambda o: op_ms[o])
     achieved = BYTES[dom] / (op_ms[dom] * 1e-3) / 1e9
@@ -538,7 +542,7 @@ def run_suite(args) -> None:
         fn = lib.rtc_fill_normal if normal else lib.rtc_fill_uniform
         N.check(fn(pair[1].ref, seed, 0, a, b))
 
-    def timeit(name, cfg, nbytes, fn):
+    def timeit(name, cfg, nbytes, fn, elems=None):
         for _ in range(2):
             fn()
         times = []
@@ -552,8 +556,15 @@ def run_suite(args) -> None:
             times.append(e0.elapsed_time(e1))
         ms = statistics.median(times)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        print(json.dumps({"op": name, "config": cfg, "ms": ms, "GB_s": gbs,
-                          "frac_of_measured_peak": gbs / peak, "bytes": nbytes}), flush=True)
+        row = {"op": name, "config": cfg, "ms": ms, "GB_s": gbs,
+               "frac_of_measured_peak": gbs / peak, "frac_of_8TBs_spec": gbs / SPEC_HBM_GBS,
+               "bytes": nbytes}
+        if elems is None:
+            elems = {"cfg1": N1, "cfg2": N2, "cfg3": R3 * C3, "cfg4": R4 * C4,
+                     "cfg5": N5}.get(cfg[:4])
+        if elems:
+            row["elements_per_s"] = elems / (ms * 1e-3)
+        print(json.dumps(row), flush=True)
 
     lr, b1, b2, eps, wd, tt = ADAMW
     # cfg1
@@ -568,6 +579,9 @@ def run_suite(args) -> None:
            lambda: N.check(lib.rtc_mul_scalar(a[1].ref, 0.5, c[1].ref)))
     timeit("add->mul_scalar (fused)", f"cfg1 [{N1}]", 12 * N1,
            lambda: N.check(lib.rtc_add_mul_scalar(a[1].ref, b[1].ref, 0.5, c[1].ref)))
+    timeit("add then mul_scalar (two kernels)", f"cfg1 [{N1}]", 20 * N1,
+           lambda: (N.check(lib.rtc_add(a[1].ref, b[1].ref, c[1].ref)),
+                    N.check(lib.rtc_mul_scalar(c[1].ref, 0.5, c[1].ref))))
     # losses (ops/loss.rs) on cfg1's shape: the ordered f32 chains are
     # serial, so these are bound by n/8 (or n) dependent adds, not by HBM
     v1 = c_double()
@@ -591,6 +605,9 @@ def run_suite(args) -> None:
                      ("min", lib.rtc_min)):
         timeit(name + " (host result)", f"cfg2 [{N2}]", 4 * N2,
                lambda fn=fn: N.check(fn(x[1].ref, byref(v))))
+    st4 = (c_double * 4)()
+    timeit("stats: sum+mean+max+min, one pass (host result)", f"cfg2 [{N2}]", 4 * N2,
+           lambda: N.check(lib.rtc_stats(x[1].ref, st4)))
     del x
     # cfg3
     x = t([R3, C3])

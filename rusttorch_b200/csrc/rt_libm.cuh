@@ -112,6 +112,17 @@ RT_HD float fdiv(float a, float b) {
   return a / b;
 #endif
 }
+// 1/a correctly rounded.  IEEE division 1/a is by definition the correctly
+// rounded reciprocal, so this equals fdiv(1, a) for every a (NaN, infinities,
+// zeros and subnormals included); the device reciprocal instruction sequence
+// is shorter than the general division's.
+RT_HD float frcp(float a) {
+#if defined(__CUDA_ARCH__)
+  return __frcp_rn(a);
+#else
+  return 1.0f / a;
+#endif
+}
 RT_HD float fsqrt(float a) {
 #if defined(__CUDA_ARCH__)
   return __fsqrt_rn(a);

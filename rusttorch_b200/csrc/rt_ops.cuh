@@ -20,8 +20,16 @@ struct OpAddMulScalar {
 };
 
 // ---- scalar: elementwise.rs:200 add_scalar, :213 mul_scalar --------------
-struct OpAddScalar { float s; RT_HD float operator()(float x) const { return fadd(x, s); } };
-struct OpMulScalar { float s; RT_HD float operator()(float x) const { return fmul(x, s); } };
+struct OpAddScalar {
+  static constexpr bool kLight = true;
+  float s;
+  RT_HD float operator()(float x) const { return fadd(x, s); }
+};
+struct OpMulScalar {
+  static constexpr bool kLight = true;
+  float s;
+  RT_HD float operator()(float x) const { return fmul(x, s); }
+};
 
 // ---- ternary: simd.rs:275 fused_multiply_add = a*b + c, two roundings ------
 struct OpFma {
@@ -31,15 +39,19 @@ struct OpFma {
 // ---- activations: activation.rs -------------------------------------------
 // :8 relu = x.max(0.0): maxnum(x, 0.0) lowers to (x > 0 ? x : 0.0) on x86_64,
 // so NaN -> +0 and -0 -> +0.
-struct OpRelu { RT_HD float operator()(float x) const { return x > 0.0f ? x : 0.0f; } };
+struct OpRelu {
+  static constexpr bool kLight = true;
+  RT_HD float operator()(float x) const { return x > 0.0f ? x : 0.0f; }
+};
 // :170 leaky_relu
 struct OpLeakyRelu {
+  static constexpr bool kLight = true;
   float alpha;
   RT_HD float operator()(float x) const { return x > 0.0f ? x : fmul(alpha, x); }
 };
 // :21 sigmoid = 1 / (1 + exp(-x))
 struct OpSigmoid {
-  RT_HD float operator()(float x) const { return fdiv(1.0f, fadd(1.0f, expf_glibc(-x))); }
+  RT_HD float operator()(float x) const { return frcp(fadd(1.0f, expf_glibc(-x))); }
 };
 // :40 tanh
 struct OpTanh { RT_HD float operator()(float x) const { return tanhf_glibc(x); } };
