@@ -422,3 +422,16 @@ def binary_cross_entropy_loss(predictions: Tensor, targets: Tensor, epsilon: flo
 
 def cross_entropy_loss(predictions: Tensor, targets: Tensor, epsilon: float = 1e-7) -> float:
     return _loss(lib().rtc_cross_entropy_loss, predictions, targets, float(epsilon))
+
+
+# ---- one process, several GPUs ---------------------------------------------
+def sharded_stats(shards) -> tuple[float, float, float, float]:
+    """(sum, mean, max, min) of the concatenation of `shards` (Tensors, each
+    on its own GPU or not), every shard summarised on its device at once."""
+    shards = list(shards)
+    arr = (_native.RtcTensor * (len(shards) or 1))()
+    for i, t in enumerate(shards):
+        arr[i] = t._desc.s
+    out = (c_double * 4)()
+    check(lib().rtc_sharded_stats(arr, len(shards), out))
+    return out[0], out[1], out[2], out[3]

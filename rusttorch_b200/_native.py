@@ -122,6 +122,7 @@ _SIGNATURES = {
     "rtc_sgd_momentum_update": (RtcResult, [T, T, T, c_double, c_double, T, T]),
     "rtc_shard_summary_local": (RtcResult, [T, POINTER(ShardSummary)]),
     "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
+    "rtc_sharded_stats": (RtcResult, [POINTER(RtcTensor), c_size_t, POINTER(c_double)]),
     "rtc_add_broadcast": (RtcResult, [T, T, T]),
     "rtc_sub_broadcast": (RtcResult, [T, T, T]),
     "rtc_mul_broadcast": (RtcResult, [T, T, T]),

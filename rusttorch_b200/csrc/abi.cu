@@ -13,6 +13,8 @@
 #include "rt_internal.h"
 #include "rt_staging.h"
 
+#include <algorithm>
+#include <thread>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -565,6 +567,42 @@ extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard
 // The reference folds max/min over the whole tensor in index order
 // (reduction.rs:36-40, :58-62); composing the shards' summaries in shard
 // order gives the same value.
+// One process, several GPUs: every shard is summarised by its own host
+// thread (so the devices work at once), then the summaries are folded in
+// shard order.  Waits first for all work already queued on the shards'
+// devices, since the shards may come from other streams.
+extern "C" rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shards,
+                                        double out[4]) {
+  if (!out) return invalid_argument("out", "must not be null");
+  if (n_shards > 0 && !shards) return invalid_argument("shards", "must not be null");
+  for (size_t i = 0; i < n_shards; i++) TRY(check_desc(&shards[i], "shard"));
+  std::vector<int> devices;
+  for (size_t i = 0; i < n_shards; i++)
+    if (shards[i].device >= 0 &&
+        std::find(devices.begin(), devices.end(), shards[i].device) == devices.end())
+      devices.push_back(shards[i].device);
+  for (int d : devices) {
+    DeviceScope scope(d);
+    if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return backend_error("cudaDeviceSynchronize", e);
+  }
+  std::vector<rtc_shard_summary> parts(n_shards);
+  std::vector<rtc_result> res(n_shards);
+  std::vector<std::thread> workers;
+  workers.reserve(n_shards);
+  for (size_t i = 0; i < n_shards; i++)
+    workers.emplace_back([&, i] { res[i] = rtc_shard_summary_local(&shards[i], &parts[i]); });
+  for (auto& w : workers) w.join();
+  rtc_result first_error = ok();
+  for (size_t i = 0; i < n_shards; i++) {
+    if (!res[i].success && first_error.success) first_error = res[i];
+    else if (!res[i].success) std::free(res[i].error_msg);
+  }
+  if (!first_error.success) return first_error;
+  return rtc_shard_combine(parts.data(), n_shards, out);
+}
+
 extern "C" rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]) {
   if (!out) return invalid_argument("out", "must not be null");
   if (n > 0 && !parts) return invalid_argument("parts", "must not be null");

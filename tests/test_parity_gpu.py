@@ -283,6 +283,30 @@ def test_reduction_at_misaligned_offset():
     assert bits(rt.max(v)) == bits(O.scalar_reduce("max", x)[1])
 
 
+def test_sharded_stats_one_process():
+    """rtc_sharded_stats over shards (on every visible GPU, round-robin) equals
+    the reference's reductions of the whole tensor."""
+    import torch
+    ngpu = max(1, torch.cuda.device_count())
+    n = 10_000_003
+    x = O.normal(n, 49)
+    x[4_000_000] = np.nan
+    cuts = [0, 1, 2_500_000, 2_500_000, 7_000_000, n]      # includes empty shards
+    shards = [rt.Tensor.from_numpy(np.ascontiguousarray(x[a:b]), device=i % ngpu)
+              for i, (a, b) in enumerate(zip(cuts[:-1], cuts[1:]))]
+    s, mean, mx, mn = rt.sharded_stats(shards)
+    assert np.isnan(s) and np.isnan(mean)
+    assert bits(np.float32(mx)) == bits(O.scalar_reduce("max", x)[1])
+    assert bits(np.float32(mn)) == bits(O.scalar_reduce("min", x)[1])
+    y = O.normal(n, 50)
+    shards = [rt.Tensor.from_numpy(np.ascontiguousarray(y[a:b]), device=i % ngpu)
+              for i, (a, b) in enumerate(zip(cuts[:-1], cuts[1:]))]
+    s, mean, mx, mn = rt.sharded_stats(shards)
+    _check_sum(s, y)
+    assert bits(np.float32(mx)) == bits(O.scalar_reduce("max", y)[1])
+    assert bits(np.float32(mn)) == bits(O.scalar_reduce("min", y)[1])
+
+
 # ---------------------------------------------------------------- cfg 3
 @pytest.mark.parametrize("op", ["sum", "max", "mean"])
 @pytest.mark.parametrize("dim", [0, 1])
