@@ -42,14 +42,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One bounded probe of the phase.  The suspend-time hint lets the hardware
+// park the thread (up to ~10 us) until the phase completes instead of
+// spinning, so a waiting warp takes no issue slots from working ones.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(10000u)
       : "memory");
   return ok != 0;
 }
