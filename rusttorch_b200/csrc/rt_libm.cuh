@@ -18,10 +18,11 @@
 //    [-ln2/2, ln2/2], exponent reconstruction by k), and fdlibm's tanhf on top
 //    of it (tanh = 1 - 2/(expm1(2|x|)+2) for |x| >= 1, -t/(t+2) with
 //    t = expm1(-2|x|) below).  Single precision, one rounding per operation.
-//  * logf_cr — log in double, rounded once to float.  glibc's logf uses a
-//    16-entry table this file does not restate; the double-rounded result
-//    differs from glibc by one ulp on about 0.02% of inputs (softplus and mish
-//    are the only users, and their tolerance says so).
+//  * logf_cr — log in double from this file's own 32-entry table (logf_tab),
+//    rounded once to float; it equals a double log rounded to float on every
+//    input.  glibc's logf uses a 16-entry table this file does not restate;
+//    the result differs from glibc by one ulp on about 0.02% of inputs
+//    (softplus, mish and the bce/ce losses use it, and their tolerances say so).
 //
 // The constants below are the ones those algorithms publish; they have to be
 // the same for the results to be bit-identical.  Both restatements were
@@ -392,9 +393,88 @@ RT_HD float tanhf_ref(float x) {
   return neg ? -z : z;
 }
 
-// logf rounded once from a double log (see the file comment).  A
+// log for f32 arguments, evaluated in double from a 32-entry table, then
+// rounded once to float (logf_tab).  x = 2^k * z with z in [0.699, 1.398)
+// (the exponent split offset by 0x3f330000, so that z stays near 1 and
+// log(x) near x = 1 comes out of r = z - 1 exactly); z's interval i (the top
+// five mantissa bits after the offset) has centre c_i (c = 1 for the interval
+// holding 1.0), invc_i = 1/c_i rounded to double and logc_i = -log(invc_i)
+// rounded to double (computed with 60-digit decimal arithmetic).  Then
+//   r = z*invc_i - 1 (one fused rounding), |r| < 0.024,
+//   log(x) = k*ln2 + logc_i + log1p(r), log1p by its Taylor series to r^7
+// (truncation below 2^-40 relative).  The double result is within ~2^-40
+// of log(x), so rounding it to float gives the correctly rounded logf except
+// within 2^-40 of a rounding boundary; over all positive floats it equals
+// (float)log((double)x) (checked exhaustively by tests/native/libm_check).
+#define RT_LOG_INVC_TABLE \
+  {0x3ff6a13cd1537290ULL, 0x3ff623fa77016240ULL, 0x3ff5ac056b015ac0ULL, 0x3ff5390948f40febULL, \
+   0x3ff4cab88725af6eULL, 0x3ff460cbc7f5cf9aULL, 0x3ff3fb013fb013fbULL, 0x3ff3991c2c187f63ULL, \
+   0x3ff33ae45b57bcb2ULL, 0x3ff2e025c04b8097ULL, 0x3ff288b01288b013ULL, 0x3ff23456789abcdfULL, \
+   0x3ff1e2ef3b3fb874ULL, 0x3ff19453808ca29cULL, 0x3ff1485f0e0acd3bULL, 0x3ff0fef010fef011ULL, \
+   0x3ff0b7e6ec259dc8ULL, 0x3ff073260a47f7c6ULL, 0x3ff03091b51f5e1aULL, 0x3ff0000000000000ULL, \
+   0x3feecc07b301ecc0ULL, 0x3fede5d6e3f8868aULL, 0x3fed0cb58f6ec074ULL, 0x3fec3f8f01c3f8f0ULL, \
+   0x3feb7d6c3dda338bULL, 0x3feac5701ac5701bULL, 0x3fea16d3f97a4b02ULL, 0x3fe970e4f80cb872ULL, \
+   0x3fe8d3018d3018d3ULL, 0x3fe83c977ab2beddULL, 0x3fe7ad2208e0ecc3ULL, 0x3fe724287f46debcULL}
+#define RT_LOG_LOGC_TABLE \
+  {0xbfd630030b3aac48ULL, 0xbfd4c9e09e172c3dULL, 0xbfd36b6776be1116ULL, 0xbfd214456d0eb8d5ULL, \
+   0xbfd0c42d676162e2ULL, 0xbfcef5ade4dcffe5ULL, 0xbfcc6ffbc6f00f71ULL, 0xbfc9f6c407089663ULL, \
+   0xbfc7898d85444c74ULL, 0xbfc527e5e4a1b58dULL, 0xbfc2d1610c86813dULL, 0xbfc08598b59e3a07ULL, \
+   0xbfbc885801bc4b20ULL, 0xbfb8197e2f40e3f0ULL, 0xbfb3bdf5a7d1ee5eULL, 0xbfaeea31c006b87cULL, \
+   0xbfa67c94f2d4bb65ULL, 0xbf9c63d2ec14aad7ULL, 0xbf882448a388a283ULL, 0x0000000000000000ULL, \
+   0x3fa39e87b9febd68ULL, 0x3fb16536eea37ae3ULL, 0x3fb8c345d6319b23ULL, 0x3fbfec9131dbeabcULL, \
+   0x3fc371fc201e8f75ULL, 0x3fc6d60fe719d21bULL, 0x3fca23bc1fe2b561ULL, 0x3fcd5c216b4fbb94ULL, \
+   0x3fd0402594b4d041ULL, 0x3fd1c898c16999fbULL, 0x3fd347dd9a987d56ULL, 0x3fd4be5f957778a1ULL}
+
+static const uint64_t kLogInvcHost[32] = RT_LOG_INVC_TABLE;
+static const uint64_t kLogLogcHost[32] = RT_LOG_LOGC_TABLE;
+#if defined(__CUDACC__)
+__device__ __align__(256) const uint64_t kLogInvcDev[32] = RT_LOG_INVC_TABLE;
+__device__ __align__(256) const uint64_t kLogLogcDev[32] = RT_LOG_LOGC_TABLE;
+#endif
+
+RT_HD double log_table_invc(uint32_t i) {
+#if defined(__CUDA_ARCH__)
+  return u2d(__ldg(&kLogInvcDev[i]));
+#else
+  return u2d(kLogInvcHost[i]);
+#endif
+}
+RT_HD double log_table_logc(uint32_t i) {
+#if defined(__CUDA_ARCH__)
+  return u2d(__ldg(&kLogLogcDev[i]));
+#else
+  return u2d(kLogLogcHost[i]);
+#endif
+}
+
+RT_HD float logf_tab(float x) {
+  uint32_t ix = f2u(x);
+  if (ix - 0x00800000u >= 0x7f800000u - 0x00800000u) {   // not a positive normal
+    if ((ix & 0x7fffffffu) == 0) return u2f(0xff800000u);  // log(+-0) = -inf
+    if (ix == 0x7f800000u) return x;                        // log(+inf) = +inf
+    if (ix > 0x7f800000u && ix < 0x80000000u) return fadd(x, x);   // NaN
+    if (ix >> 31) return u2f(0x7fc00000u);                  // x < 0: NaN
+    ix = f2u(fmul(x, 8388608.0f)) - (23u << 23);            // subnormal: x * 2^23
+  }
+  const uint32_t tmp = ix - 0x3f330000u;
+  const uint32_t i = (tmp >> 18) & 31u;
+  const int k = (int32_t)tmp >> 23;
+  const double z = (double)u2f(ix - (tmp & 0xff800000u));
+  const double r = dfma(z, log_table_invc(i), -1.0);
+  double q = dfma(r, 1.0 / 7.0, -1.0 / 6.0);
+  q = dfma(r, q, 0.2);
+  q = dfma(r, q, -0.25);
+  q = dfma(r, q, 1.0 / 3.0);
+  q = dfma(r, q, -0.5);
+  const double lead = dfma((double)k, 0x1.62e42fefa39efp-1, log_table_logc(i));
+  const double y = dadd(lead, dfma(dmul(r, r), q, r));
+  return (float)y;
+}
+
+// logf rounded once from a double-precision log (see the file comment):
+// logf_tab, which equals (float)log((double)x) for every float x.  A
 // single-precision logf (1 ulp) is not accurate enough: mish amplifies its
 // error past 4 ulp.
-RT_HD float logf_cr(float x) { return (float)log((double)x); }
+RT_HD float logf_cr(float x) { return logf_tab(x); }
 
 }  // namespace rt

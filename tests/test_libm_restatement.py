@@ -21,7 +21,7 @@ SRC = ROOT / "tests" / "native" / "libm_check.cpp"
 HDR = ROOT / "rusttorch_b200" / "csrc" / "rt_libm.cuh"
 LIB = ROOT / "_build" / "libm_check.so"
 
-NAMES = {0: "expf", 1: "expm1f", 2: "tanhf", 3: "logf"}
+NAMES = {0: "expf", 1: "expm1f", 2: "tanhf", 3: "logf", 4: "logf_tab vs double log"}
 
 
 @pytest.fixture(scope="module")
@@ -72,3 +72,16 @@ def test_logf_within_one_ulp(chk):
     n, _ = _mismatches(chk, 3, 0x00800000, 0x7f800000, 4099)
     total = (0x7f800000 - 0x00800000) // 4099
     assert n / total < 1e-3
+
+
+def test_logf_tab_equals_double_log(chk):
+    # The table-driven log (rounded once from double) against a double log
+    # rounded to float: identical on every input checked, special values,
+    # subnormals and negatives included (RT_EXHAUSTIVE=1: all 2^32).
+    exhaustive = os.environ.get("RT_EXHAUSTIVE") == "1"
+    n, first = _mismatches(chk, 4, 0, 1 << 32, 1 if exhaustive else 211)
+    assert n == 0, f"logf_tab: {n} mismatches, first at 0x{first:08x}"
+    for u in SPECIALS + [0x00000002, 0x00400000, 0x007fffff, 0x3f7fffff, 0x3f800001, 0x3f330000,
+                         0x3fb2ffff, 0x3fb30000, 0x7f7fffff, 0xbf800000]:
+        n, _ = _mismatches(chk, 4, u, u + 1, 1)
+        assert n == 0, f"logf_tab differs at 0x{u:08x}"
