@@ -263,7 +263,7 @@ rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard_summary* o
  * writes out[0] = 0 and returns RTC_EMPTY_TENSOR. */
 rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]);
 /* One process driving several GPUs: summarise every shard on its own device
- * (concurrently, one host thread per shard) and fold the summaries in shard
+ * (concurrently, one host thread per device) and fold the summaries in shard
  * order; out[4] = {sum, mean, max, min} of the concatenated tensor.  Waits
  * for the work already queued on the shards' devices first.  No reference
  * counterpart (the reference has no multi-device path); it is the

@@ -567,9 +567,9 @@ extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard
 // The reference folds max/min over the whole tensor in index order
 // (reduction.rs:36-40, :58-62); composing the shards' summaries in shard
 // order gives the same value.
-// One process, several GPUs: every shard is summarised by its own host
-// thread (so the devices work at once), then the summaries are folded in
-// shard order.  Waits first for all work already queued on the shards'
+// One process, several GPUs: the shards of each device are summarised by
+// one host thread per device (so the devices work at once), then the
+// summaries are folded in shard order.  Waits first for all work already queued on the shards'
 // devices, since the shards may come from other streams.
 extern "C" rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shards,
                                         double out[4]) {
@@ -587,12 +587,28 @@ extern "C" rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shard
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return backend_error("cudaDeviceSynchronize", e);
   }
+  // One worker per device (host-memory shards form their own group), each
+  // summarising its shards in order.
   std::vector<rtc_shard_summary> parts(n_shards);
-  std::vector<rtc_result> res(n_shards);
+  std::vector<rtc_result> res(n_shards, ok());
+  std::vector<std::vector<size_t>> groups;
+  std::vector<int> group_device;
+  for (size_t i = 0; i < n_shards; i++) {
+    const int d = shards[i].device;
+    size_t g = 0;
+    while (g < group_device.size() && group_device[g] != d) g++;
+    if (g == group_device.size()) {
+      group_device.push_back(d);
+      groups.emplace_back();
+    }
+    groups[g].push_back(i);
+  }
   std::vector<std::thread> workers;
-  workers.reserve(n_shards);
-  for (size_t i = 0; i < n_shards; i++)
-    workers.emplace_back([&, i] { res[i] = rtc_shard_summary_local(&shards[i], &parts[i]); });
+  workers.reserve(groups.size());
+  for (const auto& idx : groups)
+    workers.emplace_back([&, idx] {
+      for (size_t i : idx) res[i] = rtc_shard_summary_local(&shards[i], &parts[i]);
+    });
   for (auto& w : workers) w.join();
   rtc_result first_error = ok();
   for (size_t i = 0; i < n_shards; i++) {

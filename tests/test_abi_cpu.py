@@ -184,3 +184,16 @@ def test_descriptor_sanity():
 
 def test_python_mirror_raises_valueerror_subclass():
     assert issubclass(N.RusttorchError, ValueError)
+
+
+def test_sharded_stats_argument_checks_without_gpu():
+    import ctypes as C
+    L = N.lib()
+    out = (C.c_double * 4)()
+    r = L.rtc_sharded_stats(None, 0, out)          # nothing to reduce: the reference's
+    assert not r.success and r.code == N.EMPTY_TENSOR   # empty-tensor error for max/min
+    L.rtc_free_error_message(r.error_msg)
+    assert out[0] == 0.0
+    r = L.rtc_sharded_stats(None, 2, out)
+    assert not r.success and r.code == N.INVALID_ARGUMENT
+    L.rtc_free_error_message(r.error_msg)
