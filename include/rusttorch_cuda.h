@@ -103,7 +103,9 @@ void rtc_free_error_message(char* msg);
  * selects the per-thread default stream. */
 rtc_result rtc_set_stream(void* stream);
 void* rtc_get_stream(void);
-/* Waits for the calling thread's stream. */
+/* Waits for the calling thread's stream on its current GPU (rtc_set_device),
+ * then reports RTC_BACKEND_ERROR if a kernel on that GPU gave up one of its
+ * bounded waits since the last call (its results are then incomplete). */
 rtc_result rtc_synchronize(void);
 int rtc_device_count(void);
 /* The calling thread's current GPU (host-memory ops and the flat *_f32 API
