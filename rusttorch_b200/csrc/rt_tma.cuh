@@ -2,8 +2,8 @@
 //
 // Every wait is bounded: mbar_wait gives up after kWaitLimitNs of
 // %globaltimer time and returns false, so a kernel whose copy never lands
-// records an error and returns instead of spinning.  No load here uses
-// cluster multicast.
+// records an error and returns instead of spinning.  Every load here fills
+// the shared memory of the one CTA that issues it.
 #pragma once
 #include <cuda.h>
 #include <cstdint>
