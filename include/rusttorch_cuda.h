@@ -107,6 +107,12 @@ void* rtc_get_stream(void);
  * then reports RTC_BACKEND_ERROR if a kernel on that GPU gave up one of its
  * bounded waits since the last call (its results are then incomplete). */
 rtc_result rtc_synchronize(void);
+/* Failure-path self-test (no reference counterpart): queues a one-thread
+ * kernel on the current GPU whose bounded mbarrier wait runs out after 50 ms,
+ * as a TMA consumer's would if its tile never landed.  The next
+ * rtc_synchronize returns RTC_BACKEND_ERROR for it; the context stays usable
+ * and the call after that returns RTC_OK.  Nothing faults or hangs. */
+rtc_result rtc_selftest_bounded_wait(void);
 int rtc_device_count(void);
 /* The calling thread's current GPU (host-memory ops and the flat *_f32 API
  * run there). */

@@ -123,6 +123,7 @@ _SIGNATURES = {
     "rtc_shard_summary_local": (RtcResult, [T, POINTER(ShardSummary)]),
     "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
     "rtc_sharded_stats": (RtcResult, [POINTER(RtcTensor), c_size_t, POINTER(c_double)]),
+    "rtc_selftest_bounded_wait": (RtcResult, []),
     "rtc_add_broadcast": (RtcResult, [T, T, T]),
     "rtc_sub_broadcast": (RtcResult, [T, T, T]),
     "rtc_mul_broadcast": (RtcResult, [T, T, T]),

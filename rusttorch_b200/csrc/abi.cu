@@ -64,6 +64,13 @@ extern "C" rtc_result rtc_synchronize(void) {
   return ok();
 }
 
+extern "C" rtc_result rtc_selftest_bounded_wait(void) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return backend_error("cudaGetDevice", e);
+  return launched(launch_bounded_wait_probe(device, thread_stream()), "selftest_bounded_wait");
+}
+
 extern "C" int rtc_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;

@@ -57,13 +57,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+// Waits for the phase with the given parity to complete; false after
+// limit_ns of %globaltimer time.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, unsigned parity,
+                                              unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  return mbar_wait_for(bar, parity, kWaitLimitNs);
 }
 
 // A [box] tile of a 3-D tensor map at coordinates (c0 innermost, c1, c2)
@@ -89,5 +94,8 @@ int* wait_timeout_flag(int device);
 // Host: nonzero if a kernel on `device` gave up a bounded wait since the
 // last call (the flag is cleared).  Synchronises the device's work first.
 int take_wait_timeouts(int device);
+// Host: launches a one-thread kernel whose bounded wait runs out (50 ms), to
+// exercise the timeout path: the next rtc_synchronize reports it.
+cudaError_t launch_bounded_wait_probe(int device, cudaStream_t s);
 
 }  // namespace rt

@@ -75,4 +75,25 @@ int take_wait_timeouts(int device) {
   return v;
 }
 
+namespace {
+
+// One thread waits (50 ms at most) on an mbarrier that nothing arrives on,
+// exactly as a consumer whose tile never lands would, and takes the same
+// exit: it raises the device flag and returns.
+__global__ void bounded_wait_probe_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  if (!mbar_wait_for(&bar, 0, 50ull * 1000 * 1000)) atomicExch(err, 1);
+}
+
+}  // namespace
+
+cudaError_t launch_bounded_wait_probe(int device, cudaStream_t s) {
+  int* err = wait_timeout_flag(device);
+  if (!err) return cudaErrorInvalidValue;
+  bounded_wait_probe_kernel<<<1, 1, 0, s>>>(err);
+  return cudaGetLastError();
+}
+
 }  // namespace rt

@@ -463,3 +463,22 @@ def test_device_shard_summaries_match_and_combine():
             want = O.scalar_reduce(op, x)[1]
             assert (np.isnan(got) and np.isnan(want)) or \
                 np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32), (name, op)
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives():
+    """The failure path of the TMA rings' bounded waits, made to run out on
+    purpose: a one-thread kernel waits 50 ms on an mbarrier nothing arrives
+    on, raises the device flag and returns; rtc_synchronize reports it once,
+    and the GPU keeps working (no fault, no hang)."""
+    import ctypes
+    L = N.lib()
+    N.check(L.rtc_synchronize())
+    N.check(L.rtc_selftest_bounded_wait())
+    r = L.rtc_synchronize()
+    assert not r.success and r.code == N.BACKEND_ERROR
+    msg = ctypes.string_at(r.error_msg).decode()
+    L.rtc_free_error_message(r.error_msg)
+    assert "gave up waiting" in msg
+    N.check(L.rtc_synchronize())                      # the flag was cleared
+    x = O.normal(1 << 20, 61)
+    assert_bits_equal(rt.relu(dev(x)).to_numpy(), O.unary("relu", x), "relu after the probe")
