@@ -482,3 +482,32 @@ def test_bounded_wait_timeout_is_reported_and_context_survives():
     N.check(L.rtc_synchronize())                      # the flag was cleared
     x = O.normal(1 << 20, 61)
     assert_bits_equal(rt.relu(dev(x)).to_numpy(), O.unary("relu", x), "relu after the probe")
+
+
+def test_concurrent_host_threads():
+    """Four host threads issuing ops at once (each on its own per-thread
+    stream, ctypes releasing the GIL): every result matches the oracle."""
+    import threading
+    errors = []
+
+    def work(k):
+        try:
+            x = O.normal(256 * 1024, 70 + k).reshape(256, 1024)
+            y = O.normal(256 * 1024, 80 + k).reshape(256, 1024)
+            for _ in range(5):
+                dx, dy = dev(x), dev(y)
+                assert_bits_equal(rt.softmax(dx, 1).to_numpy(), O.softmax(x, 1), f"t{k} softmax")
+                assert_bits_equal(rt.add(dx, dy).to_numpy(), O.binary("add", x, y), f"t{k} add")
+                assert_bits_equal(rt.sum_dim(dx, 0).to_numpy(), O.reduce_dim("sum", x, 0),
+                                  f"t{k} sum_dim")
+                _check_sum(rt.sum(dx), x)
+        except Exception as e:          # collected and re-raised below
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(k,)) for k in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    if errors:
+        raise errors[0]
