@@ -546,6 +546,72 @@ lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
   if (chain) out[lane0 + tid] = acc;
 }
 
+// ------------------------------------------------ last-axis sum, warp per lane
+// One warp per lane, reading its row front to back with 16-byte loads (like
+// lane_max_kernel): tiles of 256 floats, kLwAhead tiles in flight in
+// registers, each tile passed through a per-warp shared buffer so that lanes
+// 0..7 can run ndarray's eight chains over it in order.  Only __syncwarp
+// couples the threads.  Needs len % 4 == 0 and a 16-byte-aligned base.
+constexpr int kLwWarps = 8;
+constexpr int kLwTile = 256;
+constexpr int kLwAhead = 4;
+
+__global__ void __launch_bounds__(kLwWarps * 32)
+lane_sum8_warp_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  __shared__ __align__(16) float tile_buf[kLwWarps][kLwTile];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t r = (size_t)blockIdx.x * kLwWarps + warp;
+  if (r >= lanes) return;                              // whole warp leaves together
+  float* buf = tile_buf[warp];
+  const float* row = x + r * len;
+  const size_t steps = len / 8;
+  const size_t ntiles = (8 * steps + kLwTile - 1) / kLwTile;   // tiles holding chain steps
+  const size_t n4 = len / 4;
+  auto load = [&](size_t t, float4* v) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const size_t c = t * (kLwTile / 4) + lane + 32 * h;   // float4 index in the row
+      v[h] = c < n4 ? __ldcs(reinterpret_cast<const float4*>(row) + c)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 pre[kLwAhead][2];
+#pragma unroll
+  for (int d = 0; d < kLwAhead; d++) load(d, pre[d]);
+  const int j = lane & 7;
+  float p = 0.0f;
+  for (size_t t0 = 0; t0 < ntiles; t0 += kLwAhead) {
+#pragma unroll
+    for (int d = 0; d < kLwAhead; d++) {
+      const size_t t = t0 + d;
+      if (t < ntiles) {
+        reinterpret_cast<float4*>(buf)[lane] = pre[d][0];
+        reinterpret_cast<float4*>(buf)[lane + 32] = pre[d][1];
+        load(t + kLwAhead, pre[d]);
+        __syncwarp();
+        if (lane < 8) {
+          const int n = (int)min((size_t)(kLwTile / 8), steps - t * (kLwTile / 8));
+          fold_pipelined(buf + j, 8, n, [&](float v) { p = fadd(p, v); });
+        }
+        __syncwarp();
+      }
+    }
+  }
+  float q[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) q[k] = __shfl_sync(0xffffffffu, p, k);
+  if (lane == 0) {
+    float acc = 0.0f;
+    acc = fadd(acc, fadd(q[0], q[4]));
+    acc = fadd(acc, fadd(q[1], q[5]));
+    acc = fadd(acc, fadd(q[2], q[6]));
+    acc = fadd(acc, fadd(q[3], q[7]));
+    for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, row[t]);
+    if (mean) acc = fdiv(acc, (float)len);
+    out[r] = acc;
+  }
+}
+
 // Any layout: one thread per output, sequential over len (row order).
 template <int OP>
 __global__ void __launch_bounds__(kThreads)
@@ -640,6 +706,14 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     if (op == kDimMax) {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
       lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 1024) {
+      const size_t grid = (lanes + kLwWarps - 1) / kLwWarps;
+      for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+        const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+        lane_sum8_warp_kernel<<<(unsigned)ng, kLwWarps * 32, 0, s>>>(
+            x + g0 * kLwWarps * len, lanes - g0 * kLwWarps, len, out + g0 * kLwWarps,
+            op == kDimMean);
+      }
     } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
       const size_t grid = (lanes + kLsRows - 1) / kLsRows;
       // deepest ring whose CTAs are all resident in one wave (else 4)

@@ -344,6 +344,21 @@ def test_tma_strip_shapes(shape, dim, op):
     assert_bits_equal(got, O.reduce_dim(op, x, dim), f"{op}_dim {shape} dim={dim}")
 
 
+@pytest.mark.parametrize("shape", [(13, 1028), (1, 1024), (1000, 2052), (7, 8196), (4099, 4096),
+                                   (3, 5, 1100)])
+@pytest.mark.parametrize("op", ["sum", "mean"])
+def test_last_axis_sum_warp_kernel(shape, op):
+    """Last-axis sums of rows of >= 1024 floats (the warp-per-lane kernel):
+    ragged last tiles, a tail of len % 8 elements, lanes not a multiple of
+    the eight warps per block, NaN and -0.0 in the data."""
+    x = O.normal(int(np.prod(shape)), 62, 0, 2).reshape(shape)
+    flat = x.reshape(-1, shape[-1])
+    flat[0, 3] = np.nan
+    flat[-1, :] = -0.0
+    got = getattr(rt, f"{op}_dim")(dev(x), len(shape) - 1).to_numpy()
+    assert_bits_equal(got, O.reduce_dim(op, x, len(shape) - 1), f"{op}_dim {shape}")
+
+
 def test_max_dim_with_nan_and_zero_lanes():
     x = O.normal(6 * 40, 47).reshape(6, 40)
     x[0, 10] = np.nan
