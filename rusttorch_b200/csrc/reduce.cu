@@ -706,7 +706,10 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     if (op == kDimMax) {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
       lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
-    } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 1024) {
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 1024 &&
+               lanes >= (size_t)sm_count(cur_device()) * 28) {
+      // enough lanes for ~28 warps per SM (fewer leave the warp kernel
+      // under-occupied; the staged kernel below spreads 4 lanes per CTA)
       const size_t grid = (lanes + kLwWarps - 1) / kLwWarps;
       for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
         const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
