@@ -171,8 +171,19 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
   const size_t strips = (inner + W - 1) / W;
   const size_t ctas = outer * strips;
   if (ctas >= (1ull << 31)) return cudaSuccess;
-  const size_t R = rows_for(W);
-  const size_t smem = smem_for(W);
+  size_t R = rows_for(W);
+  size_t stage = smem_for(W) / S;
+  // With at most two CTAs per SM (few, narrow strips: e.g. 4096 columns
+  // folded over many rows) each CTA can take tiles of 256 rows and a deeper
+  // ring at no cost in residency, keeping two CTAs' rings within an SM.
+  int stages = S;
+  if (ctas <= 2 * (size_t)sms) {
+    const size_t half = (size_t)(227u << 10) / 2 - 1024;   // one of two CTAs per SM
+    R = std::min<size_t>({len, 256, std::max<size_t>(8, half / 2 / (W * sizeof(float)))});
+    stage = ((R * W * sizeof(float) + kStageAlign - 1) / kStageAlign) * kStageAlign;
+    stages = (int)std::min<size_t>(kMaxStages, std::max<size_t>(2, half / stage));
+  }
+  const size_t smem = stage * stages;
   if (smem > (227u << 10)) return cudaSuccess;
 
   CUtensorMap tm;
@@ -190,7 +201,7 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
                              (int)smem);                                                     \
     if (e != cudaSuccess) return e;                                                          \
     strip_tma_kernel<OPV><<<(unsigned)ctas, threads, smem, st>>>(tm, x, len, inner, (int)W,  \
-                                                                 (int)R, S, strips, out, err); \
+                                                                 (int)R, stages, strips, out, err); \
     break;
     RT_STRIP_TMA(kDimSum)
     RT_STRIP_TMA(kDimMean)
