@@ -148,9 +148,11 @@ RT_HD double dadd(double a, double b) {
 }
 
 // 2^(i/32) rounded to nearest double, i = 0..31, as IEEE bit patterns.
-// (Computed independently from a 60-digit evaluation of exp(i*ln2/32).)
-// The device copy lives in global memory so that lanes indexing different
-// entries are served by L1 in one pass (constant memory would serialise them).
+// (Computed independently from a 60-digit evaluation of exp(i*ln2/32); kept
+// here as the documented source of RT_EXP2_TABLE_SPLICE below, which
+// tests/test_libm_restatement.py derives from it.)  The device copy lives in
+// global memory so that lanes indexing different entries are served by L1 in
+// one pass (constant memory would serialise them).
 #define RT_EXP2_TABLE                                                                       \
   {0x3ff0000000000000ULL, 0x3ff059b0d3158574ULL, 0x3ff0b5586cf9890fULL, 0x3ff11301d0125b51ULL, \
    0x3ff172b83c7d517bULL, 0x3ff1d4873168b9aaULL, 0x3ff2387a6e756238ULL, 0x3ff29e9df51fdee1ULL, \
@@ -161,28 +163,39 @@ RT_HD double dadd(double a, double b) {
    0x3ffae89f995ad3adULL, 0x3ffb7f76f2fb5e47ULL, 0x3ffc199bdd85529cULL, 0x3ffcb720dcef9069ULL, \
    0x3ffd5818dcfba487ULL, 0x3ffdfc97337b9b5fULL, 0x3ffea4afa2a490daULL, 0x3fff50765b6e4540ULL}
 
-static const uint64_t kExp2TableHost[32] = RT_EXP2_TABLE;
-#if defined(__CUDACC__)
-__device__ __align__(256) const uint64_t kExp2TableDev[32] = RT_EXP2_TABLE;
-#endif
+// The same table with i << 47 subtracted from entry i (modulo 2^64): adding
+// k << 47 to entry k % 32 then yields 2^(k/32) with k >> 5 added to the
+// exponent field (the low five bits of k cancel), and since k << 47 has no
+// bits below 47, only the high 32-bit word changes.
+#define RT_EXP2_TABLE_SPLICE \
+  {0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL, \
+   0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL, \
+   0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL, \
+   0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL, \
+   0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL, \
+   0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL, \
+   0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL, \
+   0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL}
 
-RT_HD uint64_t exp2_table(uint32_t i) {
+#if defined(__CUDACC__)
+__device__ __align__(256) const uint64_t kExp2SpliceDev[32] = RT_EXP2_TABLE_SPLICE;
+#endif
+static const uint64_t kExp2SpliceHost[32] = RT_EXP2_TABLE_SPLICE;
+
+// 2^(k/32) for the integer k in the low bits of ki.
+RT_HD double exp2_k32(uint64_t ki) {
 #if defined(__CUDA_ARCH__)
-  return __ldg(&kExp2TableDev[i]);
+  const uint64_t t = __ldg(&kExp2SpliceDev[ki & 31u]);
+  return __hiloint2double((int)((uint32_t)(t >> 32) + ((uint32_t)ki << 15)), (int)(uint32_t)t);
 #else
-  return kExp2TableHost[i];
+  const uint64_t t = kExp2SpliceHost[ki & 31u];
+  return u2d(t + (ki << 47));
 #endif
 }
 
-// expf, bit-identical to glibc's (see the file comment).
-RT_HD float expf_glibc(float x) {
-  const uint32_t top = (f2u(x) >> 20) & 0x7ffu;
-  if (top >= 0x42bu) {                 // |x| >= 88, or x is Inf/NaN
-    if (f2u(x) == 0xff800000u) return 0.0f;   // exp(-inf) = 0
-    if (top >= 0x7f8u) return fadd(x, x);     // +inf or NaN
-    if (x > u2f(0x42b17217u)) return u2f(0x7f800000u);  // overflow -> +inf
-    if (x < u2f(0xc2cff1b4u)) return 0.0f;              // underflow -> +0
-  }
+// The main path of expf_glibc for an argument already known to be finite and
+// in range (or NaN).
+RT_HD float expf_glibc_core(float x) {
   const double kInvLn2x32 = 0x1.71547652b82fep+0 * 32.0;
   const double kShift = 0x1.8p+52;
   // Cubic for 2^(r/32), |r| <= 1/2 (coefficients pre-scaled by 32^-k).
@@ -194,16 +207,34 @@ RT_HD float expf_glibc(float x) {
   const uint64_t ki = d2u(kd);
   kd = dadd(kd, -kShift);
   const double r = dfma(kInvLn2x32, xd, -kd);
-  const uint32_t idx = (uint32_t)(ki & 31u);
-  // scale = 2^(k/32): table mantissa with k>>5 added to the exponent field.
-  const uint64_t sbits = exp2_table(idx) - ((uint64_t)idx << 47) + (ki << 47);
-  const double s = u2d(sbits);
+  const double s = exp2_k32(ki);
   const double p = dfma(kC0, r, kC1);
   const double r2 = dmul(r, r);
   double y = dfma(kC2, r, 1.0);
   y = dfma(p, r2, y);
   y = dmul(y, s);
   return (float)y;
+}
+
+// expf, bit-identical to glibc's (see the file comment), without branches:
+// glibc returns +inf for x above 88.7228 and +0 below -103.97 from special
+// cases; here x is clamped to [-104, 89] instead (NaN passes both
+// comparisons), and the core path rounds exp(89) to +inf and exp(-104) to +0,
+// so every input gives glibc's result (checked over all 2^32 floats).  A
+// branch-free exp lets the compiler schedule the f64 steps of several
+// elements together.
+RT_HD float expf_glibc(float x) {
+  const float lo = x < -104.0f ? -104.0f : x;
+  return expf_glibc_core(lo > 89.0f ? 89.0f : lo);
+}
+
+// expf for x <= 0 or NaN (softmax's x - max), without expf_glibc's range
+// branches: x below -104 (including -inf) is replaced by -104, whose exp the
+// core path rounds to +0 exactly as glibc's underflow branch returns for
+// every x below -103.97; a NaN passes the comparison and comes out NaN.
+// Equal to expf_glibc on every such input (checked exhaustively on the host).
+RT_HD float expf_glibc_nonpos(float x) {
+  return expf_glibc_core(x < -104.0f ? -104.0f : x);
 }
 
 // expm1f, bit-identical to glibc's (fdlibm single-precision algorithm).
@@ -349,20 +380,15 @@ RT_HD float tanhf_common(float x) {
   return (f2u(x) >> 31) ? -z : z;
 }
 
-// tanhf, bit-identical to glibc's (fdlibm single-precision algorithm):
-// the common range through tanhf_common, the rest as fdlibm writes it.
+// tanhf, bit-identical to glibc's (fdlibm single-precision algorithm),
+// without branches: fdlibm returns +-1 for |x| >= 22 (and for +-inf) from
+// special cases, and its common path already rounds to exactly +-1 for every
+// |x| above 9.02, so x is clamped to [-21, 21] and every input goes through
+// tanhf_common (zeros, subnormals and |x| < 2^-55 come out as fdlibm's
+// x*(1+x); NaN stays NaN).  Checked against glibc over all 2^32 floats.
 RT_HD float tanhf_glibc(float x) {
-  const uint32_t jx = f2u(x);
-  const uint32_t ix = jx & 0x7fffffffu;
-  if (ix < 0x41b00000u && ix >= 0x24000000u) return tanhf_common(x);
-  const bool neg = (jx >> 31) != 0;
-  if (ix >= 0x7f800000u) {             // +-inf -> +-1, NaN -> NaN
-    const float inv = fdiv(1.0f, x);
-    return neg ? fsub(inv, 1.0f) : fadd(inv, 1.0f);
-  }
-  if (ix >= 0x41b00000u) return neg ? -1.0f : 1.0f;    // |x| >= 22: tanh rounds to +-1
-  if (ix == 0) return x;                               // +-0
-  return fmul(x, fadd(1.0f, x));                       // |x| < 2^-55
+  const float hi = x > 21.0f ? 21.0f : x;
+  return tanhf_common(hi < -21.0f ? -21.0f : hi);
 }
 
 // The branching transcription of fdlibm's tanhf, kept as the host-side
@@ -447,15 +473,8 @@ RT_HD double log_table_logc(uint32_t i) {
 #endif
 }
 
-RT_HD float logf_tab(float x) {
-  uint32_t ix = f2u(x);
-  if (ix - 0x00800000u >= 0x7f800000u - 0x00800000u) {   // not a positive normal
-    if ((ix & 0x7fffffffu) == 0) return u2f(0xff800000u);  // log(+-0) = -inf
-    if (ix == 0x7f800000u) return x;                        // log(+inf) = +inf
-    if (ix > 0x7f800000u && ix < 0x80000000u) return fadd(x, x);   // NaN
-    if (ix >> 31) return u2f(0x7fc00000u);                  // x < 0: NaN
-    ix = f2u(fmul(x, 8388608.0f)) - (23u << 23);            // subnormal: x * 2^23
-  }
+// logf_tab's path for a positive normal finite x (given as its bits).
+RT_HD float logf_tab_core(uint32_t ix) {
   const uint32_t tmp = ix - 0x3f330000u;
   const uint32_t i = (tmp >> 18) & 31u;
   const int k = (int32_t)tmp >> 23;
@@ -469,6 +488,26 @@ RT_HD float logf_tab(float x) {
   const double lead = dfma((double)k, 0x1.62e42fefa39efp-1, log_table_logc(i));
   const double y = dadd(lead, dfma(dmul(r, r), q, r));
   return (float)y;
+}
+
+RT_HD float logf_tab(float x) {
+  uint32_t ix = f2u(x);
+  if (ix - 0x00800000u >= 0x7f800000u - 0x00800000u) {   // not a positive normal
+    if ((ix & 0x7fffffffu) == 0) return u2f(0xff800000u);  // log(+-0) = -inf
+    if (ix == 0x7f800000u) return x;                        // log(+inf) = +inf
+    if (ix > 0x7f800000u && ix < 0x80000000u) return fadd(x, x);   // NaN
+    if (ix >> 31) return u2f(0x7fc00000u);                  // x < 0: NaN
+    ix = f2u(fmul(x, 8388608.0f)) - (23u << 23);            // subnormal: x * 2^23
+  }
+  return logf_tab_core(ix);
+}
+
+// logf_tab for an argument known to be a positive normal finite float or a
+// NaN (softplus's 1 + exp(x) for x <= 20): no special-case branch, a NaN is
+// returned as is by a select.
+RT_HD float logf_pos(float x) {
+  const float y = logf_tab_core(f2u(x));
+  return x != x ? x : y;
 }
 
 // logf rounded once from a double-precision log (see the file comment):

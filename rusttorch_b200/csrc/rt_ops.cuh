@@ -86,7 +86,8 @@ struct OpSelu {
 };
 // :319 softplus = x > 20 ? x : ln(1 + exp(x))
 RT_HD float softplus1(float x) {
-  return x > 20.0f ? x : logf_cr(fadd(1.0f, expf_glibc(x)));
+  // 1 + exp(x) is in [1, 4.9e8] or NaN when x <= 20, so logf_pos applies
+  return x > 20.0f ? x : logf_pos(fadd(1.0f, expf_glibc(x)));
 }
 struct OpSoftplus { RT_HD float operator()(float x) const { return softplus1(x); } };
 // :284 mish = x * tanh(softplus(x))

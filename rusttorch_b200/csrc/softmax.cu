@@ -6,6 +6,9 @@
 // with ndarray's sum_axis order: the eight-chain unrolled_fold when dim is the
 // last axis, a sequential row-order chain otherwise.
 //
+// Every exponent is x - m <= 0 (or NaN), so the exponential is
+// expf_glibc_nonpos, which skips expf's overflow branches.
+//
 // Why m may be computed with fmaxf: the fold and fmaxf agree on every lane
 // without NaN except for the sign of a zero maximum, and x - (+0) and x - (-0)
 // round to the same value for every x (x - x is +0 either way), so e is
@@ -116,7 +119,7 @@ softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
     }
   }
   m = block_max(m, red);   // contains __syncthreads: e[] is complete
-  for (size_t i = threadIdx.x; i < len; i += kRowThreads) e[i] = expf_glibc(fsub(e[i], m));
+  for (size_t i = threadIdx.x; i < len; i += kRowThreads) e[i] = expf_glibc_nonpos(fsub(e[i], m));
   __syncthreads();
   if (threadIdx.x < 8) {
     const float s = chain_sum8(e, len);
@@ -169,10 +172,10 @@ softmax_row_reg_kernel(const float* x, size_t len, float* out) {
   for (int i = 0; i < VPT; i++) {
     const int j = threadIdx.x + i * kRegThreads;
     if (j < n4) {
-      v[i].x = expf_glibc(fsub(v[i].x, m));
-      v[i].y = expf_glibc(fsub(v[i].y, m));
-      v[i].z = expf_glibc(fsub(v[i].z, m));
-      v[i].w = expf_glibc(fsub(v[i].w, m));
+      v[i].x = expf_glibc_nonpos(fsub(v[i].x, m));
+      v[i].y = expf_glibc_nonpos(fsub(v[i].y, m));
+      v[i].z = expf_glibc_nonpos(fsub(v[i].z, m));
+      v[i].w = expf_glibc_nonpos(fsub(v[i].w, m));
       es[j] = v[i];
     }
   }
@@ -226,7 +229,7 @@ row_exp_kernel(const float* x, size_t len, const float* m, float* out) {
   const float mr = m[row];
   for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < len;
        i += (size_t)gridDim.x * kRowThreads)
-    out[row * len + i] = expf_glibc(fsub(x[row * len + i], mr));
+    out[row * len + i] = expf_glibc_nonpos(fsub(x[row * len + i], mr));
 }
 
 // Long rows, pass 3: s per row, eight sequential chains (one warp per row).
@@ -262,7 +265,7 @@ softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, floa
     for (size_t l = 0; l < len; l++) m = fmaxf(m, p[l * inner]);
     float s = 0.0f;
     for (size_t l = 0; l < len; l++) {
-      const float ev = expf_glibc(fsub(p[l * inner], m));
+      const float ev = expf_glibc_nonpos(fsub(p[l * inner], m));
       q[l * inner] = ev;
       s = fadd(s, ev);
     }

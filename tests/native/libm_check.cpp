@@ -16,6 +16,8 @@ static float ref(int which, float x) {
     case 1: return expm1f(x);
     case 2: return tanhf(x);
     case 3: return logf(x);
+    case 5: return expf(x);                  // 5: expf_glibc_nonpos (x <= 0, NaN)
+    case 6: return (float)log((double)x);    // 6: logf_pos (positive normals, NaN)
     default: return (float)log((double)x);   // 4: logf_tab against a double log
   }
 }
@@ -26,6 +28,8 @@ static float mine(int which, float x) {
     case 1: return rt::expm1f_glibc(x);
     case 2: return rt::tanhf_glibc(x);
     case 3: return rt::logf_cr(x);
+    case 5: return rt::expf_glibc_nonpos(x);
+    case 6: return rt::logf_pos(x);
     default: return rt::logf_tab(x);
   }
 }

@@ -21,7 +21,8 @@ SRC = ROOT / "tests" / "native" / "libm_check.cpp"
 HDR = ROOT / "rusttorch_b200" / "csrc" / "rt_libm.cuh"
 LIB = ROOT / "_build" / "libm_check.so"
 
-NAMES = {0: "expf", 1: "expm1f", 2: "tanhf", 3: "logf", 4: "logf_tab vs double log"}
+NAMES = {0: "expf", 1: "expm1f", 2: "tanhf", 3: "logf", 4: "logf_tab vs double log",
+         5: "expf_glibc_nonpos", 6: "logf_pos"}
 
 
 @pytest.fixture(scope="module")
@@ -85,3 +86,46 @@ def test_logf_tab_equals_double_log(chk):
                          0x3fb2ffff, 0x3fb30000, 0x7f7fffff, 0xbf800000]:
         n, _ = _mismatches(chk, 4, u, u + 1, 1)
         assert n == 0, f"logf_tab differs at 0x{u:08x}"
+
+
+def test_exp2_tables():
+    # RT_EXP2_TABLE holds 2^(i/32) rounded to double; RT_EXP2_TABLE_SPLICE,
+    # which the device reads, is entry i minus i << 47 (mod 2^64).
+    import re
+    from decimal import Decimal, getcontext
+    getcontext().prec = 60
+    text = HDR.read_text()
+
+    def table(name):
+        m = re.search(r"#define " + name + r"\s*\\\n(.*?)\}", text, re.S)
+        return [int(v[:-3], 16) for v in re.findall(r"0x[0-9a-f]+ULL", m.group(1))]
+
+    plain, splice = table("RT_EXP2_TABLE"), table("RT_EXP2_TABLE_SPLICE")
+    assert len(plain) == len(splice) == 32
+    ln2 = Decimal(2).ln()
+    for i in range(32):
+        want = float((ln2 * i / 32).exp())
+        assert plain[i] == struct.unpack("<Q", struct.pack("<d", want))[0], i
+        assert splice[i] == (plain[i] - (i << 47)) % (1 << 64), i
+
+
+def test_expf_nonpos_equals_glibc(chk):
+    # every x <= 0 (sign bit set: -0 .. -inf and the negative NaNs), +0 and
+    # the positive NaNs (RT_EXHAUSTIVE=1: all of them)
+    stride = 1 if os.environ.get("RT_EXHAUSTIVE") == "1" else 211
+    n, first = _mismatches(chk, 5, 0x80000000, 1 << 32, stride)
+    assert n == 0, f"expf_glibc_nonpos: {n} mismatches, first at 0x{first:08x}"
+    n, first = _mismatches(chk, 5, 0x7f800001, 0x80000000, 4093)
+    assert n == 0, f"expf_glibc_nonpos NaN: first at 0x{first:08x}"
+    for u in (0x00000000, 0x80000000, 0xff800000, 0xc2cff1b4, 0xc2cff1b5, 0xc2d00000,
+              0xc2cfffff, 0x80000001):
+        n, _ = _mismatches(chk, 5, u, u + 1, 1)
+        assert n == 0, f"expf_glibc_nonpos differs at 0x{u:08x}"
+
+
+def test_logf_pos_on_positive_normals_and_nan(chk):
+    stride = 1 if os.environ.get("RT_EXHAUSTIVE") == "1" else 211
+    n, first = _mismatches(chk, 6, 0x00800000, 0x7f800000, stride)
+    assert n == 0, f"logf_pos: {n} mismatches, first at 0x{first:08x}"
+    n, first = _mismatches(chk, 6, 0x7f800001, 0x80000000, 4093)
+    assert n == 0, f"logf_pos NaN: first at 0x{first:08x}"
