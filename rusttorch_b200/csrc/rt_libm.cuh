@@ -367,13 +367,10 @@ RT_HD float tanhf_common(float x) {
   // 23 <= k <= 56: (xr - (e2 + 2^-k)) + 1, then 2^k scaling.
   const float two_mk = u2f((uint32_t)((0x7f - k) & 0xff) << 23);
   const float r_b = u2f(f2u(fadd(fsub(xr, fadd(e2, two_mk)), 1.0f)) + kbits);
-  float t;
-  if (ha < 0x33000000u) t = a;                          // |a| < 2^-25
-  else if (k == 0) t = r_k0;
-  else if (k == -1) t = r_km1;
-  else if (small_k) t = y_ac;
-  else if (k >= 23 && k <= 56) t = r_b;
-  else t = r_c;
+  // the reconstruction fdlibm would return, as selects (no branches)
+  const float t_big = (k >= 23 && k <= 56) ? r_b : r_c;
+  const float t_k = k == 0 ? r_k0 : (k == -1 ? r_km1 : (small_k ? y_ac : t_big));
+  const float t = ha < 0x33000000u ? a : t_k;           // |a| < 2^-25: a
   // tanh = 1 - 2/(t+2) for |x| >= 1, -t/(t+2) below: one division.
   const float q = fdiv(ge1 ? 2.0f : -t, fadd(t, 2.0f));
   const float z = ge1 ? fsub(1.0f, q) : q;
