@@ -54,9 +54,13 @@ struct OpSigmoid {
   RT_HD float operator()(float x) const { return frcp(fadd(1.0f, expf_glibc(-x))); }
 };
 // :40 tanh
-struct OpTanh { RT_HD float operator()(float x) const { return tanhf_glibc(x); } };
+struct OpTanh {
+  static constexpr bool kHeavy = true;
+  RT_HD float operator()(float x) const { return tanhf_glibc(x); }
+};
 // :61 gelu = (0.5*x) * (1 + tanh(k*(x + 0.044715*((x*x)*x)))), k = sqrt(2/pi) in f32
 struct OpGelu {
+  static constexpr bool kHeavy = true;
   float k;
   RT_HD float operator()(float x) const {
     const float x3 = fmul(fmul(x, x), x);
@@ -89,9 +93,13 @@ RT_HD float softplus1(float x) {
   // 1 + exp(x) is in [1, 4.9e8] or NaN when x <= 20, so logf_pos applies
   return x > 20.0f ? x : logf_pos(fadd(1.0f, expf_glibc(x)));
 }
-struct OpSoftplus { RT_HD float operator()(float x) const { return softplus1(x); } };
+struct OpSoftplus {
+  static constexpr bool kHeavy = true;
+  RT_HD float operator()(float x) const { return softplus1(x); }
+};
 // :284 mish = x * tanh(softplus(x))
 struct OpMish {
+  static constexpr bool kHeavy = true;
   RT_HD float operator()(float x) const { return fmul(x, tanhf_glibc(softplus1(x))); }
 };
 // :351 softsign = x / (1 + |x|)
