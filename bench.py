@@ -22,6 +22,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import re
 import os
 import statistics
 import subprocess
@@ -271,6 +272,8 @@ def main() -> None:
     ap.add_argument("--suite", action="store_true",
                     help="time every op of every config alone (L2 flushed between runs); "
                          "prints one JSON line per op")
+    ap.add_argument("--only", default="",
+                    help="with --suite: time only the ops whose name matches this regex")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: sum 2^26, softmax 8192x4096, adamw 4x2^26 (all > L2)")
     args = ap.parse_args()
@@ -542,7 +545,11 @@ def run_suite(args) -> None:
         fn = lib.rtc_fill_normal if normal else lib.rtc_fill_uniform
         N.check(fn(pair[1].ref, seed, 0, a, b))
 
+    only = re.compile(args.only) if args.only else None
+
     def timeit(name, cfg, nbytes, fn, elems=None):
+        if only is not None and not only.search(name):
+            return
         for _ in range(2):
             fn()
         times = []
@@ -582,17 +589,21 @@ def run_suite(args) -> None:
     timeit("add then mul_scalar (two kernels)", f"cfg1 [{N1}]", 20 * N1,
            lambda: (N.check(lib.rtc_add(a[1].ref, b[1].ref, c[1].ref)),
                     N.check(lib.rtc_mul_scalar(c[1].ref, 0.5, c[1].ref))))
-    # losses (ops/loss.rs) on cfg1's shape: the ordered f32 chains are
-    # serial, so these are bound by n/8 (or n) dependent adds, not by HBM
+    # losses (ops/loss.rs) on cfg1's shape: predictions uniform in [0, 1);
+    # targets uniform in [-1, 1) for the regression losses and in [0, 1) (soft
+    # labels, the cross-entropies' domain) for bce/ce
     v1 = c_double()
     fill(c, 102, False, 0.0, 1.0)
-    for name, fn, extra in (("mse_loss", lib.rtc_mse_loss, ()),
-                           ("l1_loss", lib.rtc_l1_loss, ()),
-                           ("smooth_l1_loss", lib.rtc_smooth_l1_loss, (1.0,)),
-                           ("binary_cross_entropy_loss", lib.rtc_binary_cross_entropy_loss, (1e-7,)),
-                           ("cross_entropy_loss", lib.rtc_cross_entropy_loss, (1e-7,))):
+    fill(b, 103, False, 0.0, 1.0)
+    for name, fn, extra, tg in (("mse_loss", lib.rtc_mse_loss, (), a),
+                                ("l1_loss", lib.rtc_l1_loss, (), a),
+                                ("smooth_l1_loss", lib.rtc_smooth_l1_loss, (1.0,), a),
+                                ("binary_cross_entropy_loss", lib.rtc_binary_cross_entropy_loss,
+                                 (1e-7,), b),
+                                ("cross_entropy_loss", lib.rtc_cross_entropy_loss, (1e-7,), b)):
         timeit(name, f"cfg1 [{N1}]", 8 * N1,
-               lambda fn=fn, extra=extra: N.check(fn(c[1].ref, a[1].ref, *extra, byref(v1))))
+               lambda fn=fn, extra=extra, tg=tg: N.check(fn(c[1].ref, tg[1].ref, *extra,
+                                                            byref(v1))))
     del a, b, c
     # cfg2
     x = t([N2])

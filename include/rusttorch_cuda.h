@@ -113,6 +113,13 @@ rtc_result rtc_synchronize(void);
  * rtc_synchronize returns RTC_BACKEND_ERROR for it; the context stays usable
  * and the call after that returns RTC_OK.  Nothing faults or hangs. */
 rtc_result rtc_selftest_bounded_wait(void);
+/* Test hook for the losses' ordered sum: *out_value = the f32 sum of x (f32,
+ * on a device) in ndarray's unrolled_fold order (chains = 8: eight chains over
+ * i % 8 from 0.0, combined as (p0+p4), (p1+p5), (p2+p6), (p3+p7) onto 0.0,
+ * then the remainder in order) or as one chain from init (chains = 1, the
+ * order of Iterator::sum with init = -0.0), bit for bit. */
+rtc_result rtc_selftest_ordered_sum(const rtc_tensor* x, int chains, float init,
+                                    float* out_value);
 int rtc_device_count(void);
 /* The calling thread's current GPU (host-memory ops and the flat *_f32 API
  * run there). */

@@ -263,6 +263,16 @@ static float unrolled_sum(const float* x, size_t len, size_t stride) {
   return acc;
 }
 
+float rto_unrolled_sum_f32(const float* x, size_t n) { return unrolled_sum(x, n, 1); }
+
+/* Iterator::sum::<f32>() over x: init + x[0] + x[1] + ... (init = -0.0 in the
+ * reference; core's Sum for f32 folds from -0.0). */
+float rto_chain_sum_f32(const float* x, size_t n, float init) {
+  float acc = init;
+  for (size_t i = 0; i < n; i++) acc = acc + x[i];
+  return acc;
+}
+
 static void split_dims(const size_t* shape, size_t ndim, size_t dim, size_t* outer, size_t* len,
                        size_t* inner) {
   size_t o = 1, in = 1;

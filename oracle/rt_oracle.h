@@ -129,6 +129,11 @@ void rto_fill_backward(float g, float* out, size_t n, int mean);
 int rto_reduce_to_shape(const float* grad, const size_t* gshape, size_t gnd, float* out,
                         const size_t* oshape, size_t ond);
 
+/* The two f32 sums the losses use, on their own: ndarray's sum() of a
+ * contiguous array (unrolled_fold, eight chains) and Iterator::sum from init. */
+float rto_unrolled_sum_f32(const float* x, size_t n);
+float rto_chain_sum_f32(const float* x, size_t n, float init);
+
 /* ---- loss functions: core/src/ops/loss.rs (f32 inputs) ----
  * Each returns the reference's f64 result: the f32 sum of the per-element
  * terms, as f64, divided by n.  mse/l1/smooth_l1 sum with ndarray's sum()

@@ -124,6 +124,7 @@ _SIGNATURES = {
     "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
     "rtc_sharded_stats": (RtcResult, [POINTER(RtcTensor), c_size_t, POINTER(c_double)]),
     "rtc_selftest_bounded_wait": (RtcResult, []),
+    "rtc_selftest_ordered_sum": (RtcResult, [T, c_int, c_float, POINTER(c_float)]),
     "rtc_add_broadcast": (RtcResult, [T, T, T]),
     "rtc_sub_broadcast": (RtcResult, [T, T, T]),
     "rtc_mul_broadcast": (RtcResult, [T, T, T]),

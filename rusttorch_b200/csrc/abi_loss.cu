@@ -43,14 +43,13 @@ rtc_result run_loss(LossOp op, const rtc_tensor* p, const rtc_tensor* t, float a
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
   cudaStream_t s = thread_stream();
   keep_pool_memory(p->device);
-  const size_t terms_bytes = ((n * sizeof(float)) + 255) & ~size_t(255);
+  const size_t scratch_bytes = loss_scratch_bytes(op, n);
   char* scratch = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), terms_bytes + 256, s);
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), scratch_bytes + 256, s);
   if (e != cudaSuccess) return backend_error(ctx, e);
-  float* terms = reinterpret_cast<float*>(scratch);
-  float* sum_dev = reinterpret_cast<float*>(scratch + terms_bytes);
+  float* sum_dev = reinterpret_cast<float*>(scratch + scratch_bytes);
   float sum = 0.0f;
-  e = launch_loss(op, cf(p), cf(t), n, a, b, terms, sum_dev, s);
+  e = launch_loss(op, cf(p), cf(t), n, a, b, scratch, sum_dev, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(&sum, sum_dev, sizeof sum, cudaMemcpyDeviceToHost, s);
   const cudaError_t ef = cudaFreeAsync(scratch, s);
   if (e == cudaSuccess) e = ef;
@@ -121,4 +120,40 @@ extern "C" rtc_result rtc_cross_entropy_loss(const rtc_tensor* predictions,
                                              const rtc_tensor* targets, double epsilon,
                                              double* out_value) {
   return xent(kLossCe, predictions, targets, epsilon, "cross_entropy_loss", out_value);
+}
+
+// Test hook (no reference counterpart): *out_value = the ordered f32 sum of
+// x's elements, ndarray's unrolled_fold for chains == 8, init + x[0] + x[1]
+// + ... for chains == 1 — the sums that the losses above reproduce.
+extern "C" rtc_result rtc_selftest_ordered_sum(const rtc_tensor* x, int chains, float init,
+                                               float* out_value) {
+  const char* ctx = "selftest_ordered_sum";
+  if (!out_value) return invalid_argument("out_value", "must not be null");
+  TRY(check_desc(x, "x"));
+  if (chains != 1 && chains != 8) return invalid_argument("chains", "must be 1 or 8");
+  TRY(require_f32(x, ctx));
+  if (x->device == RTC_HOST_MEMORY) return invalid_argument("device", "needs a device tensor");
+  const size_t n = x->numel;
+  if (n == 0) {
+    *out_value = chains == 8 ? 0.0f : init;
+    return ok();
+  }
+  DeviceScope scope(x->device);
+  if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
+  cudaStream_t s = thread_stream();
+  keep_pool_memory(x->device);
+  const size_t scratch_bytes = loss_scratch_bytes(chains == 8 ? kLossMse : kLossBce, n);
+  char* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), scratch_bytes + 256, s);
+  if (e != cudaSuccess) return backend_error(ctx, e);
+  float* sum_dev = reinterpret_cast<float*>(scratch + scratch_bytes);
+  float sum = 0.0f;
+  e = launch_ordered_sum_of(cf(x), n, chains, init, scratch, sum_dev, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&sum, sum_dev, sizeof sum, cudaMemcpyDeviceToHost, s);
+  const cudaError_t ef = cudaFreeAsync(scratch, s);
+  if (e == cudaSuccess) e = ef;
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return backend_error(ctx, e);
+  *out_value = sum;
+  return ok();
 }

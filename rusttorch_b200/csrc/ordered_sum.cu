@@ -1,0 +1,459 @@
+// ordered_sum.cu — the reference's sequential f32 sums of loss terms
+// (ndarray's eight-chain unrolled_fold, or Iterator::sum's one chain),
+// bit-exact and in parallel.  The algebra is in rt_osum.cuh.
+//
+// After a term kernel has written the terms (chain-major) and one f64 sum per
+// 256-element block of each chain:
+//   1. osum_chunk_kernel,  — per chain, an f64 prefix of the block sums (two
+//      osum_code_kernel      wide passes: sums per 1024 blocks, then a scan
+//                            inside each chunk); each block gets two
+//                            candidate binade codes from its estimated start
+//                            and end (rt_osum.cuh, Pair);
+//   2. osum_summary_kernel — per block, the translation runs of its 256 terms
+//                            under both codes (integer arithmetic on the
+//                            bits), and per group of 32 blocks their
+//                            composition under the first block's two codes;
+//   3. osum_walk_kernel    — one warp per chain carries the running f32 sum
+//                            across the groups, 32 at a time (the run whose
+//                            code is the sum's binade, warp scan, ballot for
+//                            the first that does not apply), then across
+//                            blocks, and folds a block whose runs do not
+//                            apply with plain f32 adds in order (where the
+//                            sum really crosses a power of two).  The first
+//                            warp then combines the chains as unrolled_fold
+//                            does and adds ndarray's remainder.
+#include "rt_internal.h"
+#include "rt_fold.cuh"
+#include "rt_libm.cuh"
+#include "rt_osum.cuh"
+
+#include <algorithm>
+
+namespace rt {
+namespace osum {
+namespace {
+
+constexpr int kCodeThreads = kChunk;
+constexpr int kSummWarps = 8;  // each warp of a group's CTA takes 4 of its blocks
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__device__ __forceinline__ int binade_code(int e, bool neg) {
+  return neg ? -(e + kCodeBias) : e + kCodeBias;
+}
+
+// The two candidate codes of a block whose chain sum is estimated to run from
+// start to end (f64).
+__device__ __forceinline__ int2 classify(double start, double end) {
+  if (start == 0.0 && end == 0.0) return make_int2(kCodeZero, kCodePoison);
+  const uint64_t a = (uint64_t)__double_as_longlong(start);
+  const uint64_t b = (uint64_t)__double_as_longlong(end);
+  if (start == 0.0 || end == 0.0 || (a >> 63) != (b >> 63))
+    return make_int2(kCodePoison, kCodePoison);
+  const bool neg = (a >> 63) != 0;
+  const int ea = (int)((a >> 52) & 0x7ff) - 1023, eb = (int)((b >> 52) & 0x7ff) - 1023;
+  const int lo = min(ea, eb), hi = max(ea, eb);
+  if (lo < -126 || hi > 127) return make_int2(kCodePoison, kCodePoison);  // also NaN/inf
+  if (hi == lo + 1) return make_int2(binade_code(ea, neg), binade_code(eb, neg));
+  if (hi != lo) return make_int2(kCodePoison, kCodePoison);
+  // one binade: the neighbour on the nearer side (log scale: the middle of
+  // the block's range against 2^e * sqrt(2))
+  const double mid = fabs(0.5 * (start + end));
+  const bool upper = mid >= ldexp(1.4142135623730951, ea);
+  const int other = upper ? ea + 1 : ea - 1;
+  const bool ok = other >= -126 && other <= 127;
+  return make_int2(binade_code(ea, neg), ok ? binade_code(other, neg) : kCodePoison);
+}
+
+// CTA-wide (1024 threads) inclusive f64 scan; returns this thread's
+// inclusive value and *total = the CTA's sum.
+__device__ __forceinline__ double cta_scan(double v, double* wsum, double* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += y;
+  }
+  if (lane == 31) wsum[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    double w = wsum[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += y;
+    }
+    wsum[lane] = w;
+  }
+  __syncthreads();
+  *total = wsum[31];
+  return v + (warp > 0 ? wsum[warp - 1] : 0.0);
+}
+
+// grid (chunks, chains): csum[c][k] = the sum of chunk k's 1024 block sums.
+__global__ void __launch_bounds__(kCodeThreads) osum_chunk_kernel(Plan plan) {
+  __shared__ double wsum[32];
+  const int c = blockIdx.y;
+  const size_t b = (size_t)blockIdx.x * kChunk + threadIdx.x;
+  const double v = b < plan.blocks ? plan.bsum[c * plan.blocks + b] : 0.0;
+  double total;
+  cta_scan(v, wsum, &total);
+  if (threadIdx.x == 0) plan.csum[c * plan.chunks + blockIdx.x] = total;
+}
+
+// grid (chunks, chains): each block's estimated start (the f64 sum of the
+// block sums before it) and end, and the codes they give.
+__global__ void __launch_bounds__(kCodeThreads) osum_code_kernel(Plan plan) {
+  __shared__ double wsum[32];
+  __shared__ double base_sh;
+  const int c = blockIdx.y;
+  const size_t k = blockIdx.x;
+  if (threadIdx.x < 32) {
+    double acc = 0.0;
+    for (size_t j = threadIdx.x; j < k; j += 32) acc += plan.csum[c * plan.chunks + j];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (threadIdx.x == 0) base_sh = acc;
+  }
+  const size_t b = k * kChunk + threadIdx.x;
+  const double v = b < plan.blocks ? plan.bsum[c * plan.blocks + b] : 0.0;
+  double total;
+  const double incl = cta_scan(v, wsum, &total);  // syncs, so base_sh is visible
+  const double end = base_sh + incl;
+  if (b < plan.blocks) plan.code[c * plan.blocks + b] = classify(end - v, end);
+}
+
+__device__ __forceinline__ Summ shfl_summ(const Summ& a, int src) {
+  Summ r;
+  r.code = __shfl_sync(0xffffffffu, a.code, src);
+  r.t0 = __shfl_sync(0xffffffffu, a.t0, src);
+  r.lo0 = __shfl_sync(0xffffffffu, a.lo0, src);
+  r.hi0 = __shfl_sync(0xffffffffu, a.hi0, src);
+  r.neg = __shfl_sync(0xffffffffu, a.neg, src);
+  r.t1 = __shfl_sync(0xffffffffu, a.t1, src);
+  r.lo1 = __shfl_sync(0xffffffffu, a.lo1, src);
+  r.hi1 = __shfl_sync(0xffffffffu, a.hi1, src);
+  return r;
+}
+
+__device__ __forceinline__ Summ shfl_down_summ(const Summ& a, int off) {
+  Summ r;
+  r.code = __shfl_down_sync(0xffffffffu, a.code, off);
+  r.t0 = __shfl_down_sync(0xffffffffu, a.t0, off);
+  r.lo0 = __shfl_down_sync(0xffffffffu, a.lo0, off);
+  r.hi0 = __shfl_down_sync(0xffffffffu, a.hi0, off);
+  r.neg = __shfl_down_sync(0xffffffffu, a.neg, off);
+  r.t1 = __shfl_down_sync(0xffffffffu, a.t1, off);
+  r.lo1 = __shfl_down_sync(0xffffffffu, a.lo1, off);
+  r.hi1 = __shfl_down_sync(0xffffffffu, a.hi1, off);
+  return r;
+}
+
+__device__ __forceinline__ Summ shfl_up_summ(const Summ& a, int off) {
+  Summ r;
+  r.code = __shfl_up_sync(0xffffffffu, a.code, off);
+  r.t0 = __shfl_up_sync(0xffffffffu, a.t0, off);
+  r.lo0 = __shfl_up_sync(0xffffffffu, a.lo0, off);
+  r.hi0 = __shfl_up_sync(0xffffffffu, a.hi0, off);
+  r.neg = __shfl_up_sync(0xffffffffu, a.neg, off);
+  r.t1 = __shfl_up_sync(0xffffffffu, a.t1, off);
+  r.lo1 = __shfl_up_sync(0xffffffffu, a.lo1, off);
+  r.hi1 = __shfl_up_sync(0xffffffffu, a.hi1, off);
+  return r;
+}
+
+// Lane 0 gets lane 0's, then 1's, ..., then 31's run composed in lane order.
+__device__ __forceinline__ Summ warp_compose(Summ a) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const Summ b = shfl_down_summ(a, off);
+    if ((threadIdx.x & 31) + off < 32) a = summ_compose(a, b);
+  }
+  return a;
+}
+
+// Lane l gets lanes 0..l composed in order.
+__device__ __forceinline__ Summ warp_scan(Summ a) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const Summ b = shfl_up_summ(a, off);
+    if (lane >= off) a = summ_compose(b, a);
+  }
+  return a;
+}
+
+__device__ __forceinline__ Summ load_summ(const Summ* p) {
+  const int4 a = __ldcg(reinterpret_cast<const int4*>(p));
+  const int4 b = __ldcg(reinterpret_cast<const int4*>(p) + 1);
+  return Summ{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+}
+
+__device__ __forceinline__ void store_summ(Summ* p, const Summ& s) {
+  reinterpret_cast<int4*>(p)[0] = make_int4(s.code, s.t0, s.lo0, s.hi0);
+  reinterpret_cast<int4*>(p)[1] = make_int4(s.neg, s.t1, s.lo1, s.hi1);
+}
+
+// One-parity run (a block without ties): moves t, partial extremes lo/hi.
+struct Run1 {
+  int t, lo, hi;
+};
+
+__device__ __forceinline__ Run1 run1_compose(const Run1& a, const Run1& b) {
+  return Run1{clamp_sat(a.t + b.t), min(a.lo, clamp_sat(a.t + b.lo)),
+              max(a.hi, clamp_sat(a.t + b.hi))};
+}
+
+// Warp: the run of one block's terms (x: lane's 8 elements, elements past
+// the block's end already replaced by 0 — they move by 0, so their partial
+// sums repeat the last real one and change nothing) under a binade code.
+__device__ __forceinline__ Summ block_run(const float (&x)[8], int cd) {
+  const int lane = threadIdx.x & 31;
+  const int e = (cd < 0 ? -cd : cd) - kCodeBias;
+  int m0[8], m1[8];
+  bool tie = false;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    tau_pair(x[k], e, m0[k], m1[k]);
+    tie |= m0[k] != m1[k];
+  }
+  if (!__any_sync(0xffffffffu, tie)) {
+    Run1 r{0, kLoId, kHiId};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {  // |partial| <= 8 * 2^26: no overflow
+      r.t += m0[k];
+      r.lo = min(r.lo, r.t);
+      r.hi = max(r.hi, r.t);
+    }
+    r = Run1{clamp_sat(r.t), clamp_sat(r.lo), clamp_sat(r.hi)};
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Run1 o{__shfl_down_sync(0xffffffffu, r.t, off),
+                   __shfl_down_sync(0xffffffffu, r.lo, off),
+                   __shfl_down_sync(0xffffffffu, r.hi, off)};
+      if (lane + off < 32) r = run1_compose(r, o);
+    }
+    return Summ{cd, r.t, r.lo, r.hi, 0, r.t, r.lo, r.hi};
+  }
+  Summ mine = summ_make(cd);
+#pragma unroll
+  for (int k = 0; k < 8; k++) summ_push(mine, m0[k], m1[k]);
+  return warp_compose(mine);
+}
+
+__device__ __forceinline__ Summ pick(const Pair& p, int cd) {
+  if (p.a.code == kCodeNone) return p.a;
+  return p.a.code == cd ? p.a : (p.b.code == cd ? p.b : summ_make(kCodePoison));
+}
+
+// grid (groups, chains), 8 warps: each warp takes 4 of the group's blocks and
+// computes their runs under both codes; warp 0 then composes the group under
+// the first block's two codes.
+__global__ void __launch_bounds__(32 * kSummWarps) osum_summary_kernel(Plan plan) {
+  __shared__ Pair runs[kGroup];
+  const int c = blockIdx.y;
+  const size_t g = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = 0; i < kGroup / kSummWarps; i++) {
+    const int wb = warp + kSummWarps * i;
+    const size_t b = g * kGroup + wb;
+    Pair pr{summ_make(kCodeNone), summ_make(kCodeNone)};
+    if (b < plan.blocks) {
+      const size_t first = b * kBlock;
+      const int cnt = (int)min((size_t)kBlock, plan.len - first);
+      const float* tb = plan.terms + c * plan.pitch + first;
+      const int j0 = 8 * lane;
+      // the chain pitch is a multiple of the block, so whole blocks are in bounds
+      const float4 x0 = __ldcs(reinterpret_cast<const float4*>(tb + j0));
+      const float4 x1 = __ldcs(reinterpret_cast<const float4*>(tb + j0 + 4));
+      float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = j0 + k < cnt ? x[k] : 0.0f;
+      const int2 cd = plan.code[c * plan.blocks + b];
+      if (cd.x == kCodeZero) {
+        bool allzero = true, allneg = true;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const uint32_t u = __float_as_uint(x[k]);
+          allzero &= (u & 0x7fffffffu) == 0;
+          allneg &= j0 + k >= cnt || u == 0x80000000u;
+        }
+        pr.a = summ_make(__all_sync(0xffffffffu, allzero) ? kCodeZero : kCodePoison);
+        pr.a.neg = __all_sync(0xffffffffu, allneg) ? 1 : 0;
+        pr.b = summ_make(kCodePoison);
+      } else {
+        pr.a = cd.x != kCodePoison ? block_run(x, cd.x) : summ_make(kCodePoison);
+        pr.b = cd.y != kCodePoison ? block_run(x, cd.y) : summ_make(kCodePoison);
+      }
+      if (lane == 0) {
+        Pair* dst = plan.l0 + c * plan.blocks + b;
+        store_summ(&dst->a, pr.a);
+        store_summ(&dst->b, pr.b);
+      }
+    }
+    if (lane == 0) runs[wb] = pr;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const Pair mine = runs[lane];
+    const int c1 = runs[0].a.code, c2 = runs[0].b.code;
+    const Summ g1 = warp_compose(pick(mine, c1));
+    const Summ g2 = c2 != kCodePoison ? warp_compose(pick(mine, c2)) : summ_make(kCodePoison);
+    if (lane == 0) {
+      Pair* dst = plan.l1 + c * plan.groups + g;
+      store_summ(&dst->a, g1);
+      store_summ(&dst->b, g2);
+    }
+  }
+}
+
+// The code of the binade s lies in (kCodeZero for +-0; poison for
+// subnormal, inf and NaN, which no run applies to).
+__device__ __forceinline__ int code_of(float s) {
+  const uint32_t u = __float_as_uint(s);
+  const int ex = (int)((u >> 23) & 0xffu);
+  if ((u & 0x7fffffffu) == 0) return kCodeZero;
+  if (ex == 0 || ex == 0xff) return kCodePoison;
+  return binade_code(ex - 127, (u >> 31) != 0);
+}
+
+__device__ __forceinline__ Summ load_pick(const Pair* p, bool valid, int cd) {
+  if (!valid) return summ_make(kCodePoison);
+  const Summ a = load_summ(&p->a);
+  const Summ b = load_summ(&p->b);
+  return a.code == cd ? a : (b.code == cd ? b : summ_make(kCodePoison));
+}
+
+// Folds block b of chain c in order onto s (one lane adds; all lanes return it).
+__device__ __forceinline__ float fold_block(const Plan& plan, float* buf, int c, size_t b,
+                                            float s) {
+  const int lane = threadIdx.x & 31;
+  const size_t first = b * kBlock;
+  const int cnt = (int)min((size_t)kBlock, plan.len - first);
+  const float4* tb = reinterpret_cast<const float4*>(plan.terms + c * plan.pitch + first);
+  reinterpret_cast<float4*>(buf)[lane] = __ldcg(tb + lane);
+  reinterpret_cast<float4*>(buf)[lane + 32] = __ldcg(tb + lane + 32);
+  __syncwarp();
+  if (lane == 0) fold_pipelined(buf, 1, cnt, [&](float v) { s = fadd(s, v); });
+  s = __shfl_sync(0xffffffffu, s, 0);
+  __syncwarp();
+  return s;
+}
+
+// One step over up to 32 runs (lane l: the run at position l, already picked
+// for s's binade): applies the longest prefix that provably applies.  Returns
+// how many runs were applied and updates s.
+__device__ __forceinline__ int apply_prefix(const Summ& run, float& s) {
+  const Summ x = warp_scan(run);
+  float after;
+  const bool ok = summ_apply(x, s, &after);
+  const unsigned bal = __ballot_sync(0xffffffffu, ok);
+  const int k = bal == 0xffffffffu ? 32 : __ffs(~bal) - 1;
+  if (k > 0) s = __shfl_sync(0xffffffffu, after, k - 1);
+  return k;
+}
+
+// One CTA, one warp per chain.
+template <int CH>
+__global__ void __launch_bounds__(32 * CH) osum_walk_kernel(Plan plan, float init, float* out) {
+  __shared__ __align__(16) float buf[CH][kBlock];
+  __shared__ float chain_sum[CH];
+  const int c = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t nb = plan.blocks, ng = plan.groups;
+  const Pair* l0 = plan.l0 + c * nb;
+  const Pair* l1 = plan.l1 + c * ng;
+  float s = init;
+  size_t b = 0;
+  while (b < nb) {
+    if (s != s) break;  // NaN + anything stays NaN
+    const int cd = code_of(s);
+    if ((b % kGroup) == 0) {
+      const size_t g0 = b / kGroup;
+      const int k = apply_prefix(load_pick(l1 + g0 + lane, g0 + lane < ng, cd), s);
+      if (k > 0) {
+        b = min(nb, (g0 + k) * kGroup);
+        continue;
+      }
+    }
+    const size_t gend = min(nb, (b / kGroup + 1) * kGroup);
+    const int k = apply_prefix(load_pick(l0 + b + lane, b + lane < gend, cd), s);
+    if (k > 0) {
+      b += k;
+      continue;
+    }
+    s = fold_block(plan, buf[c], c, b, s);  // no run of block b applies
+    b++;
+  }
+  if (lane == 0) chain_sum[c] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = chain_sum[0];
+    if constexpr (CH == 8) {
+      r = 0.0f;
+      r = fadd(r, fadd(chain_sum[0], chain_sum[4]));
+      r = fadd(r, fadd(chain_sum[1], chain_sum[5]));
+      r = fadd(r, fadd(chain_sum[2], chain_sum[6]));
+      r = fadd(r, fadd(chain_sum[3], chain_sum[7]));
+      const size_t rest = plan.n - plan.len * CH;
+      for (size_t i = 0; i < rest; i++) r = fadd(r, plan.terms[CH * plan.pitch + i]);
+    }
+    out[0] = r;
+  }
+}
+
+}  // namespace
+
+Plan make_plan(void* scratch, size_t n, int chains) {
+  Plan p;
+  p.chains = chains;
+  p.n = n;
+  p.len = n / chains;
+  p.blocks = (p.len + kBlock - 1) / kBlock;
+  p.groups = (p.blocks + kGroup - 1) / kGroup;
+  p.pitch = p.blocks * kBlock;
+  p.chunks = (p.blocks + kChunk - 1) / kChunk;
+  char* at = static_cast<char*>(scratch);
+  p.terms = reinterpret_cast<float*>(at);
+  at += round_up((chains * p.pitch + 8) * sizeof(float), 256);
+  p.bsum = reinterpret_cast<double*>(at);
+  at += round_up(chains * p.blocks * sizeof(double), 256);
+  p.csum = reinterpret_cast<double*>(at);
+  at += round_up(chains * p.chunks * sizeof(double), 256);
+  p.code = reinterpret_cast<int2*>(at);
+  at += round_up(chains * p.blocks * sizeof(int2), 256);
+  p.l0 = reinterpret_cast<Pair*>(at);
+  at += round_up(chains * p.blocks * sizeof(Pair), 256);
+  p.l1 = reinterpret_cast<Pair*>(at);
+  return p;
+}
+
+size_t scratch_bytes(size_t n, int chains) {
+  const Plan p = make_plan(nullptr, n, chains);
+  return reinterpret_cast<size_t>(p.l1) + round_up(chains * p.groups * sizeof(Pair), 256);
+}
+
+int term_grid(const Plan& plan) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t tiles = (plan.len * plan.chains + kTileIn - 1) / kTileIn;
+  const size_t cap = (size_t)sm_count(dev) * 8;  // 8 CTAs of 256 threads per SM
+  return (int)std::max<size_t>(1, std::min(tiles, cap));
+}
+
+cudaError_t launch_ordered_sum(const Plan& plan, float init, float* out, cudaStream_t s) {
+  if (plan.blocks > 0) {
+    const dim3 cgrid((unsigned)plan.chunks, (unsigned)plan.chains);
+    osum_chunk_kernel<<<cgrid, kCodeThreads, 0, s>>>(plan);
+    osum_code_kernel<<<cgrid, kCodeThreads, 0, s>>>(plan);
+    const dim3 grid((unsigned)plan.groups, (unsigned)plan.chains);
+    osum_summary_kernel<<<grid, 32 * kSummWarps, 0, s>>>(plan);
+  }
+  if (plan.chains == 8)
+    osum_walk_kernel<8><<<1, 32 * 8, 0, s>>>(plan, 0.0f, out);
+  else
+    osum_walk_kernel<1><<<1, 32, 0, s>>>(plan, init, out);
+  return cudaGetLastError();
+}
+
+}  // namespace osum
+}  // namespace rt

@@ -135,10 +135,17 @@ float gelu_k();
 // ------------------------------------------------------------------- losses
 enum LossOp { kLossMse, kLossL1, kLossSmoothL1, kLossBce, kLossCe };
 // *sum_out (device) = the reference's ordered f32 sum of the loss terms of
-// p and t; `terms` is n floats of 16-byte-aligned device scratch.  a, b:
-// smooth_l1 (beta, 0.5*beta), bce (eps, 1 - eps), ce (eps, unused), in f32.
+// p and t; `scratch` is loss_scratch_bytes(op, n) bytes of 256-byte-aligned
+// device memory.  a, b: smooth_l1 (beta, 0.5*beta), bce (eps, 1 - eps), ce
+// (eps, unused), in f32.
+size_t loss_scratch_bytes(LossOp op, size_t n);
 cudaError_t launch_loss(LossOp op, const float* p, const float* t, size_t n, float a, float b,
-                        float* terms, float* sum_out, cudaStream_t s);
+                        void* scratch, float* sum_out, cudaStream_t s);
+// *sum_out (device) = x's ordered f32 sum: ndarray's unrolled_fold for
+// chains == 8, init + x[0] + x[1] + ... for chains == 1.  Scratch as for a
+// loss of the same chain count.
+cudaError_t launch_ordered_sum_of(const float* x, size_t n, int chains, float init, void* scratch,
+                                  float* sum_out, cudaStream_t s);
 
 // -------------------------------------------------------------------- softmax
 cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,

@@ -55,6 +55,8 @@ def lib():
                                         c_float, c_uint64, F, F, F]),
             "rto_nn_sgd_step": (None, [F, F, F, c_size_t, c_float, c_float, c_float, F, F]),
             "rto_broadcast_binary": (c_int, [c_int, F, sz, c_size_t, F, sz, c_size_t, F]),
+            "rto_unrolled_sum_f32": (c_float, [F, c_size_t]),
+            "rto_chain_sum_f32": (c_float, [F, c_size_t, c_float]),
             "rto_mse_loss": (c_double, [F, F, c_size_t]),
             "rto_l1_loss": (c_double, [F, F, c_size_t]),
             "rto_smooth_l1_loss": (c_double, [F, F, c_size_t, c_double]),
@@ -249,6 +251,16 @@ def reduce_to_shape(grad, shape):
 
 
 # ---- losses (ops/loss.rs) -------------------------------------------------
+def unrolled_sum_f32(x):
+    """ndarray's sum() of a contiguous f32 array (eight chains), as an f32."""
+    return np.float32(lib().rto_unrolled_sum_f32(p(x), x.size))
+
+
+def chain_sum_f32(x, init=-0.0):
+    """Iterator::sum of f32s from init, as an f32."""
+    return np.float32(lib().rto_chain_sum_f32(p(x), x.size, init))
+
+
 def loss(name, pred, targ, *param):
     """name in mse, l1, smooth_l1, bce, ce; returns the reference's f64."""
     return getattr(lib(), f"rto_{name}_loss")(p(pred), p(targ), pred.size, *map(float, param))
