@@ -10,14 +10,17 @@
 //                            candidate binade codes from its estimated start
 //                            and end (rt_osum.cuh, Pair);
 //   2. osum_summary_kernel — per block, the translation runs of its 256 terms
-//                            under both codes (integer arithmetic on the
-//                            bits), and per group of 32 blocks their
-//                            composition under the first block's two codes;
+//                            under both codes (the moves from exact f32
+//                            scaling and round-to-nearest-even, tau_pair_f),
+//                            and per group of 32 blocks their composition
+//                            under the first block's two codes;
+//      osum_super_kernel   — and per 32 groups (1024 blocks) theirs;
 //   3. osum_walk_kernel    — one warp per chain carries the running f32 sum
-//                            across the groups, 32 at a time (the run whose
+//                            across the super-groups, 32 at a time (the run whose
 //                            code is the sum's binade, warp scan, ballot for
-//                            the first that does not apply), then across
-//                            blocks, and folds a block whose runs do not
+//                            the first that does not apply), then across the
+//                            groups and blocks inside the one that does not,
+//                            and folds a block whose runs do not
 //                            apply with plain f32 adds in order (where the
 //                            sum really crosses a power of two).  The first
 //                            warp then combines the chains as unrolled_fold
@@ -35,6 +38,7 @@ namespace {
 
 constexpr int kCodeThreads = kChunk;
 constexpr int kSummWarps = 8;  // each warp of a group's CTA takes 4 of its blocks
+constexpr int kMinBinade = -100;  // 2^(23 - e) must be a normal f32
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -43,7 +47,10 @@ __device__ __forceinline__ int binade_code(int e, bool neg) {
 }
 
 // The two candidate codes of a block whose chain sum is estimated to run from
-// start to end (f64).
+// start to end (f64): the binade(s) of the estimate, plus the neighbour when
+// the estimate lies within 1/8 of a binade boundary (the f32 chain's drift
+// from the exact prefix stays far below that in practice).  Binades below
+// 2^-100 are left to the ordered fold.
 __device__ __forceinline__ int2 classify(double start, double end) {
   if (start == 0.0 && end == 0.0) return make_int2(kCodeZero, kCodePoison);
   const uint64_t a = (uint64_t)__double_as_longlong(start);
@@ -53,15 +60,12 @@ __device__ __forceinline__ int2 classify(double start, double end) {
   const bool neg = (a >> 63) != 0;
   const int ea = (int)((a >> 52) & 0x7ff) - 1023, eb = (int)((b >> 52) & 0x7ff) - 1023;
   const int lo = min(ea, eb), hi = max(ea, eb);
-  if (lo < -126 || hi > 127) return make_int2(kCodePoison, kCodePoison);  // also NaN/inf
+  if (lo < kMinBinade || hi > 127) return make_int2(kCodePoison, kCodePoison);  // also NaN/inf
   if (hi == lo + 1) return make_int2(binade_code(ea, neg), binade_code(eb, neg));
   if (hi != lo) return make_int2(kCodePoison, kCodePoison);
-  // one binade: the neighbour on the nearer side (log scale: the middle of
-  // the block's range against 2^e * sqrt(2))
   const double mid = fabs(0.5 * (start + end));
-  const bool upper = mid >= ldexp(1.4142135623730951, ea);
-  const int other = upper ? ea + 1 : ea - 1;
-  const bool ok = other >= -126 && other <= 127;
+  const int other = mid < ldexp(1.125, ea) ? ea - 1 : (mid >= ldexp(1.75, ea) ? ea + 1 : 1000);
+  const bool ok = other >= kMinBinade && other <= 127;
   return make_int2(binade_code(ea, neg), ok ? binade_code(other, neg) : kCodePoison);
 }
 
@@ -210,11 +214,12 @@ __device__ __forceinline__ Run1 run1_compose(const Run1& a, const Run1& b) {
 __device__ __forceinline__ Summ block_run(const float (&x)[8], int cd) {
   const int lane = threadIdx.x & 31;
   const int e = (cd < 0 ? -cd : cd) - kCodeBias;
+  const float scale = __uint_as_float((uint32_t)(23 - e + 127) << 23);  // 2^(23 - e)
   int m0[8], m1[8];
   bool tie = false;
 #pragma unroll
   for (int k = 0; k < 8; k++) {
-    tau_pair(x[k], e, m0[k], m1[k]);
+    tau_pair_f(x[k], scale, m0[k], m1[k]);
     tie |= m0[k] != m1[k];
   }
   if (!__any_sync(0xffffffffu, tie)) {
@@ -307,6 +312,25 @@ __global__ void __launch_bounds__(32 * kSummWarps) osum_summary_kernel(Plan plan
   }
 }
 
+// grid (supers, chains), one warp: the 32 group records of super-group q
+// composed under the first group's two codes.
+__global__ void __launch_bounds__(32) osum_super_kernel(Plan plan) {
+  const int c = blockIdx.y, lane = threadIdx.x;
+  const size_t q = blockIdx.x, g = q * kGroup + lane;
+  const Pair* src = plan.l1 + c * plan.groups;
+  Pair mine{summ_make(kCodeNone), summ_make(kCodeNone)};
+  if (g < plan.groups) mine = Pair{load_summ(&src[g].a), load_summ(&src[g].b)};
+  const int c1 = __shfl_sync(0xffffffffu, mine.a.code, 0);
+  const int c2 = __shfl_sync(0xffffffffu, mine.b.code, 0);
+  const Summ s1 = warp_compose(pick(mine, c1));
+  const Summ s2 = c2 != kCodePoison ? warp_compose(pick(mine, c2)) : summ_make(kCodePoison);
+  if (lane == 0) {
+    Pair* dst = plan.l2 + c * plan.supers + q;
+    store_summ(&dst->a, s1);
+    store_summ(&dst->b, s2);
+  }
+}
+
 // The code of the binade s lies in (kCodeZero for +-0; poison for
 // subnormal, inf and NaN, which no run applies to).
 __device__ __forceinline__ int code_of(float s) {
@@ -315,13 +339,6 @@ __device__ __forceinline__ int code_of(float s) {
   if ((u & 0x7fffffffu) == 0) return kCodeZero;
   if (ex == 0 || ex == 0xff) return kCodePoison;
   return binade_code(ex - 127, (u >> 31) != 0);
-}
-
-__device__ __forceinline__ Summ load_pick(const Pair* p, bool valid, int cd) {
-  if (!valid) return summ_make(kCodePoison);
-  const Summ a = load_summ(&p->a);
-  const Summ b = load_summ(&p->b);
-  return a.code == cd ? a : (b.code == cd ? b : summ_make(kCodePoison));
 }
 
 // Folds block b of chain c in order onto s (one lane adds; all lanes return it).
@@ -341,9 +358,48 @@ __device__ __forceinline__ float fold_block(const Plan& plan, float* buf, int c,
 }
 
 // One step over up to 32 runs (lane l: the run at position l, already picked
-// for s's binade): applies the longest prefix that provably applies.  Returns
-// how many runs were applied and updates s.
-__device__ __forceinline__ int apply_prefix(const Summ& run, float& s) {
+// for s's binade code cd; none for positions already behind, poison where the
+// step must stop): applies the longest prefix that provably applies and
+// returns the first lane that does not (32 if none).
+__device__ __forceinline__ int apply_prefix(const Summ& run, int cd, float& s) {
+  constexpr int kBig = 1 << 29;  // partial extremes are kept in [-kBig, kBig]
+  const int lane = threadIdx.x & 31;
+  if (cd == kCodePoison) return 0;  // s is subnormal or not finite: no run applies
+  const bool none = run.code == kCodeNone;
+  const bool stop = !none && run.code != cd;
+  const bool flat = none || stop || (run.t0 == run.t1 && run.lo0 == run.lo1 && run.hi0 == run.hi1);
+  if (cd != kCodeZero && __all_sync(0xffffffffu, flat)) {
+    // no run depends on parity: one inclusive scan of (moves, least partial,
+    // greatest partial), composed as (ta + tb, min(la, ta + lb), max(ha, ta + hb))
+    int t = none || stop ? 0 : run.t0;
+    int lo = none ? kBig : (stop ? -kBig : run.lo0);
+    int hi = none ? -kBig : (stop ? kBig : run.hi0);
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int ta = __shfl_up_sync(0xffffffffu, t, off);
+      const int la = __shfl_up_sync(0xffffffffu, lo, off);
+      const int ha = __shfl_up_sync(0xffffffffu, hi, off);
+      if (lane >= off) {
+        lo = min(la, min(max(ta + lo, -kBig), kBig));
+        hi = max(ha, min(max(ta + hi, -kBig), kBig));
+        t = clamp_sat(ta + t);
+      }
+    }
+    const uint32_t sb = __float_as_uint(s);
+    const bool neg = cd < 0;
+    const int mag = (int)((sb & 0x7fffffu) | 0x800000u);
+    const int S = neg ? -mag : mag;
+    constexpr int kMin = (1 << 23) + 1, kMax = (1 << 24) - 1;
+    const bool ok = neg ? (S + hi <= -kMin && S + lo >= -kMax) : (S + lo >= kMin && S + hi <= kMax);
+    const unsigned bal = __ballot_sync(0xffffffffu, ok);
+    const int k = bal == 0xffffffffu ? 32 : __ffs(~bal) - 1;
+    if (k > 0) {
+      const int r = S + __shfl_sync(0xffffffffu, t, k - 1);
+      const uint32_t rm = (uint32_t)(r < 0 ? -r : r);
+      s = __uint_as_float((sb & 0xff800000u) | (rm - 0x800000u));
+    }
+    return k;
+  }
   const Summ x = warp_scan(run);
   float after;
   const bool ok = summ_apply(x, s, &after);
@@ -353,36 +409,73 @@ __device__ __forceinline__ int apply_prefix(const Summ& run, float& s) {
   return k;
 }
 
-// One CTA, one warp per chain.
+__device__ __forceinline__ Pair load_pair(const Pair* p, bool valid) {
+  if (!valid) return Pair{summ_make(kCodePoison), summ_make(kCodePoison)};
+  return Pair{load_summ(&p->a), load_summ(&p->b)};
+}
+
+__device__ __forceinline__ Summ pick_run(const Pair& p, int cd) {
+  return p.a.code == cd ? p.a : (p.b.code == cd ? p.b : summ_make(kCodePoison));
+}
+
+// One CTA, one warp per chain.  Three levels: 32 super-groups (1024 blocks
+// each) per step, then 32 groups of the super-group that does not apply, then
+// the blocks of the group that does not apply (their records loaded once),
+// folding in order only a block none of whose runs applies.
 template <int CH>
 __global__ void __launch_bounds__(32 * CH) osum_walk_kernel(Plan plan, float init, float* out) {
+  constexpr size_t kSuper = (size_t)kGroup * kGroup;  // blocks per super-group
   __shared__ __align__(16) float buf[CH][kBlock];
   __shared__ float chain_sum[CH];
   const int c = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t nb = plan.blocks, ng = plan.groups;
+  const size_t nb = plan.blocks, ng = plan.groups, nsg = plan.supers;
   const Pair* l0 = plan.l0 + c * nb;
   const Pair* l1 = plan.l1 + c * ng;
+  const Pair* l2 = plan.l2 + c * nsg;
   float s = init;
   size_t b = 0;
+  size_t next_q0 = 0;  // super-group records of the next 32, loaded ahead
+  Pair next = load_pair(l2 + lane, lane < nsg);
   while (b < nb) {
     if (s != s) break;  // NaN + anything stays NaN
-    const int cd = code_of(s);
+    if ((b % kSuper) == 0) {
+      const size_t q0 = b / kSuper;
+      const Pair rec = q0 == next_q0 ? next : load_pair(l2 + q0 + lane, q0 + lane < nsg);
+      next_q0 = q0 + 32;
+      next = load_pair(l2 + next_q0 + lane, next_q0 + lane < nsg);
+      const int cd = code_of(s);
+      const int k = apply_prefix(pick_run(rec, cd), cd, s);
+      if (k > 0) {
+        b = min(nb, (q0 + k) * kSuper);
+        continue;
+      }
+    }
     if ((b % kGroup) == 0) {
       const size_t g0 = b / kGroup;
-      const int k = apply_prefix(load_pick(l1 + g0 + lane, g0 + lane < ng, cd), s);
+      const size_t gend = min(ng, (g0 / kGroup + 1) * kGroup);  // this super-group's end
+      const int cd = code_of(s);
+      const int k = apply_prefix(pick_run(load_pair(l1 + g0 + lane, g0 + lane < gend), cd), cd, s);
       if (k > 0) {
         b = min(nb, (g0 + k) * kGroup);
         continue;
       }
     }
-    const size_t gend = min(nb, (b / kGroup + 1) * kGroup);
-    const int k = apply_prefix(load_pick(l0 + b + lane, b + lane < gend, cd), s);
-    if (k > 0) {
-      b += k;
-      continue;
+    // the blocks of b's group
+    const size_t base = b / kGroup * kGroup;
+    const int end = (int)min((size_t)kGroup, nb - base);
+    const Pair pr = load_pair(l0 + base + lane, lane < end);
+    int pos = (int)(b - base);
+    while (pos < end && s == s) {
+      const int cd = code_of(s);
+      const int k = apply_prefix(lane < pos ? summ_make(kCodeNone) : pick_run(pr, cd), cd, s);
+      if (k > pos) {
+        pos = k;
+        continue;
+      }
+      s = fold_block(plan, buf[c], c, base + pos, s);  // no run of this block applies
+      pos++;
     }
-    s = fold_block(plan, buf[c], c, b, s);  // no run of block b applies
-    b++;
+    b = base + min(pos, end);
   }
   if (lane == 0) chain_sum[c] = s;
   __syncthreads();
@@ -410,6 +503,7 @@ Plan make_plan(void* scratch, size_t n, int chains) {
   p.len = n / chains;
   p.blocks = (p.len + kBlock - 1) / kBlock;
   p.groups = (p.blocks + kGroup - 1) / kGroup;
+  p.supers = (p.groups + kGroup - 1) / kGroup;
   p.pitch = p.blocks * kBlock;
   p.chunks = (p.blocks + kChunk - 1) / kChunk;
   char* at = static_cast<char*>(scratch);
@@ -424,12 +518,14 @@ Plan make_plan(void* scratch, size_t n, int chains) {
   p.l0 = reinterpret_cast<Pair*>(at);
   at += round_up(chains * p.blocks * sizeof(Pair), 256);
   p.l1 = reinterpret_cast<Pair*>(at);
+  at += round_up(chains * p.groups * sizeof(Pair), 256);
+  p.l2 = reinterpret_cast<Pair*>(at);
   return p;
 }
 
 size_t scratch_bytes(size_t n, int chains) {
   const Plan p = make_plan(nullptr, n, chains);
-  return reinterpret_cast<size_t>(p.l1) + round_up(chains * p.groups * sizeof(Pair), 256);
+  return reinterpret_cast<size_t>(p.l2) + round_up(chains * p.supers * sizeof(Pair), 256);
 }
 
 int term_grid(const Plan& plan) {
@@ -447,6 +543,7 @@ cudaError_t launch_ordered_sum(const Plan& plan, float init, float* out, cudaStr
     osum_code_kernel<<<cgrid, kCodeThreads, 0, s>>>(plan);
     const dim3 grid((unsigned)plan.groups, (unsigned)plan.chains);
     osum_summary_kernel<<<grid, 32 * kSummWarps, 0, s>>>(plan);
+    osum_super_kernel<<<dim3((unsigned)plan.supers, (unsigned)plan.chains), 32, 0, s>>>(plan);
   }
   if (plan.chains == 8)
     osum_walk_kernel<8><<<1, 32 * 8, 0, s>>>(plan, 0.0f, out);

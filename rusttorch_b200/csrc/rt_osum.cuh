@@ -27,6 +27,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cmath>
 #include <cstring>
 
 namespace rt {
@@ -105,6 +106,35 @@ __host__ __device__ __forceinline__ void tau_pair(float x, int e, int& m0, int& 
   const int sat = neg && ex != 0xff ? -kSat : kSat;
   m0 = big ? sat : (tie ? lo + odd_lo : rounded);
   m1 = big ? sat : (tie ? lo + (odd_lo ^ 1) : rounded);
+}
+
+// The same moves from f32 arithmetic, for a binade e in [-100, 127] given as
+// scale = 2^(23 - e) (a normal f32).  q = x * scale = x/u is exact (or, when it
+// underflows, far below 1/2); adding 1.5 * 2^23 rounds it to the nearest
+// integer, ties to even, and since that constant is even the rounded q is the
+// move for an even S.  For a tie the odd S takes the other neighbour.  Moves
+// of 2^22 or more (and NaN/inf) saturate: a run needs |move| < 2^23 to apply,
+// so this only sends terms as large as half the running sum to the ordered
+// fold.  Equal to tau_pair for every x with |x/u| < 2^22.
+__host__ __device__ __forceinline__ void tau_pair_f(float x, float scale, int& m0, int& m1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+#ifdef __CUDA_ARCH__
+  const float q = __fmul_rn(x, scale);
+  const float y = __fadd_rn(q, kMagic);
+  const float r = __fsub_rn(y, kMagic);
+  const float d = __fsub_rn(q, r);
+#else
+  const float q = x * scale;
+  const float y = q + kMagic;
+  const float r = y - kMagic;
+  const float d = q - r;
+#endif
+  const bool ok = fabsf(q) < 4194304.0f;  // 2^22; false for NaN
+  const int m = (int)(bits_of(y) - bits_of(kMagic));
+  const int odd = fabsf(d) == 0.5f ? (d > 0.0f ? 1 : -1) : 0;
+  const int sat = x < 0.0f ? -kSat : kSat;
+  m0 = ok ? m : sat;
+  m1 = ok ? m + odd : sat;
 }
 
 // Appends one element's move pair to a binade run (in order).
@@ -231,7 +261,7 @@ constexpr int kChunk = 1024;  // blocks per chunk of the binade-guess scan
 
 struct Plan {
   int chains;
-  size_t n, len, pitch, blocks, groups, chunks;
+  size_t n, len, pitch, blocks, groups, supers, chunks;
   float* terms;
   double* bsum;   // [chains][blocks] f64 block sums (binade guesses)
   double* csum;   // [chains][chunks] their sums per 1024 blocks
@@ -239,6 +269,7 @@ struct Plan {
   Pair* l0;       // [chains][blocks] the block's runs under its two codes
   Pair* l1;       // [chains][groups] the 32 blocks composed under the first
                   // block's two codes
+  Pair* l2;       // [chains][supers] 32 groups (1024 blocks) composed likewise
 };
 
 // Term kernel: terms[] and block sums of term(p[i], t[i]) for i < n, laid out
