@@ -418,16 +418,16 @@ __device__ __forceinline__ Summ pick_run(const Pair& p, int cd) {
   return p.a.code == cd ? p.a : (p.b.code == cd ? p.b : summ_make(kCodePoison));
 }
 
-// One CTA, one warp per chain.  Three levels: 32 super-groups (1024 blocks
+// One CTA (one warp) per chain, so that every chain's latency-bound walk has
+// an SM to itself; the last chain to finish combines them.  Three levels: 32 super-groups (1024 blocks
 // each) per step, then 32 groups of the super-group that does not apply, then
 // the blocks of the group that does not apply (their records loaded once),
 // folding in order only a block none of whose runs applies.
 template <int CH>
-__global__ void __launch_bounds__(32 * CH) osum_walk_kernel(Plan plan, float init, float* out) {
+__global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, float* out) {
   constexpr size_t kSuper = (size_t)kGroup * kGroup;  // blocks per super-group
-  __shared__ __align__(16) float buf[CH][kBlock];
-  __shared__ float chain_sum[CH];
-  const int c = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(16) float buf[1][kBlock];
+  const int c = blockIdx.x, lane = threadIdx.x;
   const size_t nb = plan.blocks, ng = plan.groups, nsg = plan.supers;
   const Pair* l0 = plan.l0 + c * nb;
   const Pair* l1 = plan.l1 + c * ng;
@@ -472,25 +472,29 @@ __global__ void __launch_bounds__(32 * CH) osum_walk_kernel(Plan plan, float ini
         pos = k;
         continue;
       }
-      s = fold_block(plan, buf[c], c, base + pos, s);  // no run of this block applies
+      s = fold_block(plan, buf[0], c, base + pos, s);  // no run of this block applies
       pos++;
     }
     b = base + min(pos, end);
   }
-  if (lane == 0) chain_sum[c] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float r = chain_sum[0];
-    if constexpr (CH == 8) {
-      r = 0.0f;
-      r = fadd(r, fadd(chain_sum[0], chain_sum[4]));
-      r = fadd(r, fadd(chain_sum[1], chain_sum[5]));
-      r = fadd(r, fadd(chain_sum[2], chain_sum[6]));
-      r = fadd(r, fadd(chain_sum[3], chain_sum[7]));
-      const size_t rest = plan.n - plan.len * CH;
-      for (size_t i = 0; i < rest; i++) r = fadd(r, plan.terms[CH * plan.pitch + i]);
+  if (lane == 0) {
+    plan.chain_out[c] = s;
+    __threadfence();
+    if (atomicAdd(plan.done, 1u) == CH - 1) {
+      __threadfence();
+      const volatile float* cs = plan.chain_out;
+      float r = cs[0];
+      if constexpr (CH == 8) {
+        r = 0.0f;
+        r = fadd(r, fadd(cs[0], cs[4]));
+        r = fadd(r, fadd(cs[1], cs[5]));
+        r = fadd(r, fadd(cs[2], cs[6]));
+        r = fadd(r, fadd(cs[3], cs[7]));
+        const size_t rest = plan.n - plan.len * CH;
+        for (size_t i = 0; i < rest; i++) r = fadd(r, plan.terms[CH * plan.pitch + i]);
+      }
+      out[0] = r;
     }
-    out[0] = r;
   }
 }
 
@@ -520,12 +524,15 @@ Plan make_plan(void* scratch, size_t n, int chains) {
   p.l1 = reinterpret_cast<Pair*>(at);
   at += round_up(chains * p.groups * sizeof(Pair), 256);
   p.l2 = reinterpret_cast<Pair*>(at);
+  at += round_up(chains * p.supers * sizeof(Pair), 256);
+  p.chain_out = reinterpret_cast<float*>(at);
+  p.done = reinterpret_cast<unsigned*>(at + 64);
   return p;
 }
 
 size_t scratch_bytes(size_t n, int chains) {
   const Plan p = make_plan(nullptr, n, chains);
-  return reinterpret_cast<size_t>(p.l2) + round_up(chains * p.supers * sizeof(Pair), 256);
+  return reinterpret_cast<size_t>(p.chain_out) + 256;
 }
 
 int term_grid(const Plan& plan) {
@@ -546,7 +553,7 @@ cudaError_t launch_ordered_sum(const Plan& plan, float init, float* out, cudaStr
     osum_super_kernel<<<dim3((unsigned)plan.supers, (unsigned)plan.chains), 32, 0, s>>>(plan);
   }
   if (plan.chains == 8)
-    osum_walk_kernel<8><<<1, 32 * 8, 0, s>>>(plan, 0.0f, out);
+    osum_walk_kernel<8><<<8, 32, 0, s>>>(plan, 0.0f, out);
   else
     osum_walk_kernel<1><<<1, 32, 0, s>>>(plan, init, out);
   return cudaGetLastError();

@@ -270,6 +270,8 @@ struct Plan {
   Pair* l1;       // [chains][groups] the 32 blocks composed under the first
                   // block's two codes
   Pair* l2;       // [chains][supers] 32 groups (1024 blocks) composed likewise
+  float* chain_out;   // [chains] each chain's sum
+  unsigned* done;     // chains finished (zeroed by the term kernel)
 };
 
 // Term kernel: terms[] and block sums of term(p[i], t[i]) for i < n, laid out
@@ -339,6 +341,7 @@ osum_terms_kernel(const float* __restrict__ p, const float* __restrict__ t, Term
       if (lane == 0 && blk < plan.blocks) plan.bsum[blk] = acc;
     }
   }
+  if (blockIdx.x == 0 && tid == 0) *plan.done = 0u;
   // ndarray's remainder (n % 8 terms, summed after the chains)
   const size_t rest = plan.n - lim;
   if (blockIdx.x == 0 && (size_t)tid < rest)
