@@ -341,20 +341,16 @@ __device__ __forceinline__ int code_of(float s) {
   return binade_code(ex - 127, (u >> 31) != 0);
 }
 
-// Folds block b of chain c in order onto s (one lane adds; all lanes return it).
-__device__ __forceinline__ float fold_block(const Plan& plan, float* buf, int c, size_t b,
-                                            float s) {
-  const int lane = threadIdx.x & 31;
-  const size_t first = b * kBlock;
-  const int cnt = (int)min((size_t)kBlock, plan.len - first);
-  const float4* tb = reinterpret_cast<const float4*>(plan.terms + c * plan.pitch + first);
-  reinterpret_cast<float4*>(buf)[lane] = __ldcg(tb + lane);
-  reinterpret_cast<float4*>(buf)[lane + 32] = __ldcg(tb + lane + 32);
-  __syncwarp();
-  if (lane == 0) fold_pipelined(buf, 1, cnt, [&](float v) { s = fadd(s, v); });
-  s = __shfl_sync(0xffffffffu, s, 0);
-  __syncwarp();
-  return s;
+// apply_prefix for runs that depend on parity (ties) or a zero sum: the
+// full composition.
+__device__ __forceinline__ int apply_prefix_general(const Summ& run, float& s) {
+  const Summ x = warp_scan(run);
+  float after;
+  const bool ok = summ_apply(x, s, &after);
+  const unsigned bal = __ballot_sync(0xffffffffu, ok);
+  const int k = bal == 0xffffffffu ? 32 : __ffs(~bal) - 1;
+  if (k > 0) s = __shfl_sync(0xffffffffu, after, k - 1);
+  return k;
 }
 
 // One step over up to 32 runs (lane l: the run at position l, already picked
@@ -368,6 +364,7 @@ __device__ __forceinline__ int apply_prefix(const Summ& run, int cd, float& s) {
   const bool none = run.code == kCodeNone;
   const bool stop = !none && run.code != cd;
   const bool flat = none || stop || (run.t0 == run.t1 && run.lo0 == run.lo1 && run.hi0 == run.hi1);
+  constexpr int kMin = (1 << 23) + 1, kMax = (1 << 24) - 1;
   if (cd != kCodeZero && __all_sync(0xffffffffu, flat)) {
     // no run depends on parity: one inclusive scan of (moves, least partial,
     // greatest partial), composed as (ta + tb, min(la, ta + lb), max(ha, ta + hb))
@@ -389,7 +386,6 @@ __device__ __forceinline__ int apply_prefix(const Summ& run, int cd, float& s) {
     const bool neg = cd < 0;
     const int mag = (int)((sb & 0x7fffffu) | 0x800000u);
     const int S = neg ? -mag : mag;
-    constexpr int kMin = (1 << 23) + 1, kMax = (1 << 24) - 1;
     const bool ok = neg ? (S + hi <= -kMin && S + lo >= -kMax) : (S + lo >= kMin && S + hi <= kMax);
     const unsigned bal = __ballot_sync(0xffffffffu, ok);
     const int k = bal == 0xffffffffu ? 32 : __ffs(~bal) - 1;
@@ -400,13 +396,7 @@ __device__ __forceinline__ int apply_prefix(const Summ& run, int cd, float& s) {
     }
     return k;
   }
-  const Summ x = warp_scan(run);
-  float after;
-  const bool ok = summ_apply(x, s, &after);
-  const unsigned bal = __ballot_sync(0xffffffffu, ok);
-  const int k = bal == 0xffffffffu ? 32 : __ffs(~bal) - 1;
-  if (k > 0) s = __shfl_sync(0xffffffffu, after, k - 1);
-  return k;
+  return apply_prefix_general(run, s);
 }
 
 __device__ __forceinline__ Pair load_pair(const Pair* p, bool valid) {
@@ -436,6 +426,8 @@ __global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, fl
   size_t b = 0;
   size_t next_q0 = 0;  // super-group records of the next 32, loaded ahead
   Pair next = load_pair(l2 + lane, lane < nsg);
+  size_t rec1_super = ~(size_t)0;  // the super-group whose group records are in rec1
+  Pair rec1;
   while (b < nb) {
     if (s != s) break;  // NaN + anything stays NaN
     if ((b % kSuper) == 0) {
@@ -451,12 +443,17 @@ __global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, fl
       }
     }
     if ((b % kGroup) == 0) {
-      const size_t g0 = b / kGroup;
-      const size_t gend = min(ng, (g0 / kGroup + 1) * kGroup);  // this super-group's end
+      const size_t q = b / kSuper, gbase = q * kGroup;
+      if (q != rec1_super) {
+        rec1 = load_pair(l1 + gbase + lane, gbase + lane < ng);
+        rec1_super = q;
+      }
+      const int off = (int)(b / kGroup - gbase);
       const int cd = code_of(s);
-      const int k = apply_prefix(pick_run(load_pair(l1 + g0 + lane, g0 + lane < gend), cd), cd, s);
-      if (k > 0) {
-        b = min(nb, (g0 + k) * kGroup);
+      const Summ run = lane < off ? summ_make(kCodeNone) : pick_run(rec1, cd);
+      const int k = apply_prefix(run, cd, s);
+      if (k > off) {
+        b = min(nb, (gbase + k) * kGroup);
         continue;
       }
     }
@@ -467,12 +464,23 @@ __global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, fl
     int pos = (int)(b - base);
     while (pos < end && s == s) {
       const int cd = code_of(s);
-      const int k = apply_prefix(lane < pos ? summ_make(kCodeNone) : pick_run(pr, cd), cd, s);
+      const Summ run = lane < pos ? summ_make(kCodeNone) : pick_run(pr, cd);
+      const int k = apply_prefix(run, cd, s);
       if (k > pos) {
         pos = k;
         continue;
       }
-      s = fold_block(plan, buf[0], c, base + pos, s);  // no run of this block applies
+      // no run of block base + pos applies: fold it in order
+      const size_t fb = base + pos;
+      const int cnt = (int)min((size_t)kBlock, plan.len - fb * kBlock);
+      const float4* tb = reinterpret_cast<const float4*>(plan.terms + c * plan.pitch + fb * kBlock);
+      const float4 t0 = __ldcg(tb + 2 * lane), t1 = __ldcg(tb + 2 * lane + 1);
+      reinterpret_cast<float4*>(buf[0])[2 * lane] = t0;
+      reinterpret_cast<float4*>(buf[0])[2 * lane + 1] = t1;
+      __syncwarp();
+      if (lane == 0) fold_pipelined(buf[0], 1, cnt, [&](float v) { s = fadd(s, v); });
+      s = __shfl_sync(0xffffffffu, s, 0);
+      __syncwarp();
       pos++;
     }
     b = base + min(pos, end);
