@@ -546,69 +546,75 @@ lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
   if (chain) out[lane0 + tid] = acc;
 }
 
-// ------------------------------------------------ last-axis sum, warp per lane
-// One warp per lane, reading its row front to back with 16-byte loads (like
-// lane_max_kernel): tiles of 256 floats, kLwAhead tiles in flight in
-// registers, each tile passed through a per-warp shared buffer so that lanes
-// 0..7 can run ndarray's eight chains over it in order.  Only __syncwarp
-// couples the threads.  Needs len % 4 == 0 and a 16-byte-aligned base.
-constexpr int kLwWarps = 8;
-constexpr int kLwTile = 256;
-constexpr int kLwAhead = 4;
+// ------------------------------------------------ last-axis sum, 4 lanes per warp
+// Four lanes (rows) per warp, each read front to back with 16-byte loads; the
+// same eight ordered chains per row (ndarray's unrolled_fold), but all
+// 32 threads run chains (thread 8r + j runs chain j of the warp's row r), so
+// a chain step costs one warp instruction for 32 chains instead of 8.  Each
+// tile step stages 128 floats of every row through a per-warp shared buffer
+// (row pitch 136 floats: the four rows' chains read distinct banks), with the
+// next kLqAhead tiles' 16-byte loads in flight in registers.  Only
+// __syncwarp couples the threads.  Needs len % 4 == 0 and a 16-byte-aligned
+// base.
+constexpr int kLqWarps = 8;
+constexpr int kLqTile = 128;     // floats of each row per tile step
+constexpr int kLqPitch = kLqTile + 8;
+constexpr int kLqAhead = 4;
 
-__global__ void __launch_bounds__(kLwWarps * 32)
-lane_sum8_warp_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
-  __shared__ __align__(16) float tile_buf[kLwWarps][kLwTile];
+__global__ void __launch_bounds__(kLqWarps * 32)
+lane_sum8_quad_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  __shared__ __align__(16) float tile_buf[kLqWarps][4 * kLqPitch];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t r = (size_t)blockIdx.x * kLwWarps + warp;
-  if (r >= lanes) return;                              // whole warp leaves together
+  const size_t r0 = ((size_t)blockIdx.x * kLqWarps + warp) * 4;
+  if (r0 >= lanes) return;                             // whole warp leaves together
   float* buf = tile_buf[warp];
-  const float* row = x + r * len;
-  const size_t steps = len / 8;
-  const size_t ntiles = (8 * steps + kLwTile - 1) / kLwTile;   // tiles holding chain steps
+  const size_t steps = len / 8;                        // chain steps per row
+  const size_t ntiles = (8 * steps + kLqTile - 1) / kLqTile;
   const size_t n4 = len / 4;
   auto load = [&](size_t t, float4* v) {
+    const size_t c = t * (kLqTile / 4) + lane;         // float4 index in each row
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const size_t c = t * (kLwTile / 4) + lane + 32 * h;   // float4 index in the row
-      v[h] = c < n4 ? __ldcs(reinterpret_cast<const float4*>(row) + c)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int rr = 0; rr < 4; rr++) {
+      const size_t row = r0 + rr;
+      v[rr] = (c < n4 && row < lanes) ? __ldcs(reinterpret_cast<const float4*>(x + row * len) + c)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
-  float4 pre[kLwAhead][2];
+  float4 pre[kLqAhead][4];
 #pragma unroll
-  for (int d = 0; d < kLwAhead; d++) load(d, pre[d]);
-  const int j = lane & 7;
+  for (int d = 0; d < kLqAhead; d++) load(d, pre[d]);
+  const int rr = lane >> 3, j = lane & 7;
+  const float* chain = buf + rr * kLqPitch + j;
   float p = 0.0f;
-  for (size_t t0 = 0; t0 < ntiles; t0 += kLwAhead) {
+  for (size_t t0 = 0; t0 < ntiles; t0 += kLqAhead) {
 #pragma unroll
-    for (int d = 0; d < kLwAhead; d++) {
+    for (int d = 0; d < kLqAhead; d++) {
       const size_t t = t0 + d;
       if (t < ntiles) {
-        reinterpret_cast<float4*>(buf)[lane] = pre[d][0];
-        reinterpret_cast<float4*>(buf)[lane + 32] = pre[d][1];
-        load(t + kLwAhead, pre[d]);
+#pragma unroll
+        for (int q = 0; q < 4; q++) reinterpret_cast<float4*>(buf + q * kLqPitch)[lane] = pre[d][q];
+        load(t + kLqAhead, pre[d]);
         __syncwarp();
-        if (lane < 8) {
-          const int n = (int)min((size_t)(kLwTile / 8), steps - t * (kLwTile / 8));
-          fold_pipelined(buf + j, 8, n, [&](float v) { p = fadd(p, v); });
-        }
+        const int n = (int)min((size_t)(kLqTile / 8), steps - t * (kLqTile / 8));
+        fold_pipelined(chain, 8, n, [&](float v) { p = fadd(p, v); });
         __syncwarp();
       }
     }
   }
   float q[8];
 #pragma unroll
-  for (int k = 0; k < 8; k++) q[k] = __shfl_sync(0xffffffffu, p, k);
-  if (lane == 0) {
+  for (int k = 0; k < 8; k++) q[k] = __shfl_sync(0xffffffffu, p, (lane & ~7) + k);
+  const size_t row = r0 + rr;
+  if (j == 0 && row < lanes) {
     float acc = 0.0f;
     acc = fadd(acc, fadd(q[0], q[4]));
     acc = fadd(acc, fadd(q[1], q[5]));
     acc = fadd(acc, fadd(q[2], q[6]));
     acc = fadd(acc, fadd(q[3], q[7]));
-    for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, row[t]);
+    const float* xr = x + row * len;
+    for (size_t t = steps * 8; t < len; t++) acc = fadd(acc, xr[t]);
     if (mean) acc = fdiv(acc, (float)len);
-    out[r] = acc;
+    out[row] = acc;
   }
 }
 
@@ -710,11 +716,12 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
                lanes >= (size_t)sm_count(cur_device()) * 28) {
       // enough lanes for ~28 warps per SM (fewer leave the warp kernel
       // under-occupied; the staged kernel below spreads 4 lanes per CTA)
-      const size_t grid = (lanes + kLwWarps - 1) / kLwWarps;
+      const size_t per_cta = (size_t)kLqWarps * 4;      // rows
+      const size_t grid = (lanes + per_cta - 1) / per_cta;
       for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
         const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
-        lane_sum8_warp_kernel<<<(unsigned)ng, kLwWarps * 32, 0, s>>>(
-            x + g0 * kLwWarps * len, lanes - g0 * kLwWarps, len, out + g0 * kLwWarps,
+        lane_sum8_quad_kernel<<<(unsigned)ng, kLqWarps * 32, 0, s>>>(
+            x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta,
             op == kDimMean);
       }
     } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
