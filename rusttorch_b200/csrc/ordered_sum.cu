@@ -127,19 +127,6 @@ __global__ void __launch_bounds__(kCodeThreads) osum_code_kernel(Plan plan) {
   if (b < plan.blocks) plan.code[c * plan.blocks + b] = classify(end - v, end);
 }
 
-__device__ __forceinline__ Summ shfl_summ(const Summ& a, int src) {
-  Summ r;
-  r.code = __shfl_sync(0xffffffffu, a.code, src);
-  r.t0 = __shfl_sync(0xffffffffu, a.t0, src);
-  r.lo0 = __shfl_sync(0xffffffffu, a.lo0, src);
-  r.hi0 = __shfl_sync(0xffffffffu, a.hi0, src);
-  r.neg = __shfl_sync(0xffffffffu, a.neg, src);
-  r.t1 = __shfl_sync(0xffffffffu, a.t1, src);
-  r.lo1 = __shfl_sync(0xffffffffu, a.lo1, src);
-  r.hi1 = __shfl_sync(0xffffffffu, a.hi1, src);
-  return r;
-}
-
 __device__ __forceinline__ Summ shfl_down_summ(const Summ& a, int off) {
   Summ r;
   r.code = __shfl_down_sync(0xffffffffu, a.code, off);
