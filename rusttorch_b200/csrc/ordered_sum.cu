@@ -395,11 +395,44 @@ __device__ __forceinline__ Summ pick_run(const Pair& p, int cd) {
   return p.a.code == cd ? p.a : (p.b.code == cd ? p.b : summ_make(kCodePoison));
 }
 
+// With the running sum at +-inf only a NaN or the opposite infinity can change
+// it, and a block holds one exactly when its f64 block sum is NaN or that
+// opposite infinity (an f64 sum of f32 terms cannot overflow); the same holds
+// for the 1024-block chunk sums.  The first block at or after b that can
+// change s (nb if none), found from the chunk sums, then the block sums.
+__device__ __forceinline__ size_t next_inf_breaker(const Plan& plan, int c, size_t b, bool pos) {
+  const int lane = threadIdx.x & 31;
+  const double other = pos ? -INFINITY : INFINITY;
+  const double* bs = plan.bsum + c * plan.blocks;
+  const double* cs = plan.csum + c * plan.chunks;
+  const size_t nb = plan.blocks;
+  while (b < nb) {
+    if (b % kChunk == 0) {  // whole chunks
+      const size_t k0 = b / kChunk;
+      const double v = k0 + lane < plan.chunks ? __ldcg(cs + k0 + lane) : 0.0;
+      const unsigned bad = __ballot_sync(0xffffffffu, v != v || v == other);
+      if (!bad) {
+        b = min(nb, (k0 + 32) * kChunk);
+        continue;
+      }
+      b = (k0 + (__ffs(bad) - 1)) * kChunk;
+    }
+    const size_t cend = min(nb, (b / kChunk + 1) * kChunk);
+    const double v = b + lane < cend ? __ldcg(bs + b + lane) : 0.0;
+    const unsigned bad = __ballot_sync(0xffffffffu, v != v || v == other);
+    if (bad) return b + (__ffs(bad) - 1);
+    b = min(cend, b + 32);
+  }
+  return nb;
+}
+
 // One CTA (one warp) per chain, so that every chain's latency-bound walk has
-// an SM to itself; the last chain to finish combines them.  Three levels: 32 super-groups (1024 blocks
-// each) per step, then 32 groups of the super-group that does not apply, then
-// the blocks of the group that does not apply (their records loaded once),
-// folding in order only a block none of whose runs applies.
+// an SM to itself; the last chain to finish combines them.  Three levels: 32
+// super-groups (1024 blocks each) per step, then 32 groups of the super-group
+// that does not apply, then the blocks of the group that does not apply
+// (their records loaded once), folding in order only a block none of whose
+// runs applies.  A NaN sum ends the walk; an infinite one skips to the blocks
+// that can still change it.
 template <int CH>
 __global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, float* out) {
   constexpr size_t kSuper = (size_t)kGroup * kGroup;  // blocks per super-group
@@ -417,6 +450,21 @@ __global__ void __launch_bounds__(32) osum_walk_kernel(Plan plan, float init, fl
   Pair rec1;
   while (b < nb) {
     if (s != s) break;  // NaN + anything stays NaN
+    if ((__float_as_uint(s) & 0x7fffffffu) == 0x7f800000u) {
+      // +-inf: skip to the first block that can change it and fold that one
+      b = next_inf_breaker(plan, c, b, s > 0.0f);
+      if (b >= nb) break;
+      const float4* tb = reinterpret_cast<const float4*>(plan.terms + c * plan.pitch + b * kBlock);
+      reinterpret_cast<float4*>(buf[0])[2 * lane] = __ldcg(tb + 2 * lane);
+      reinterpret_cast<float4*>(buf[0])[2 * lane + 1] = __ldcg(tb + 2 * lane + 1);
+      __syncwarp();
+      const int cnt = (int)min((size_t)kBlock, plan.len - b * kBlock);
+      if (lane == 0) fold_pipelined(buf[0], 1, cnt, [&](float v) { s = fadd(s, v); });
+      s = __shfl_sync(0xffffffffu, s, 0);
+      __syncwarp();
+      b++;
+      continue;
+    }
     if ((b % kSuper) == 0) {
       const size_t q0 = b / kSuper;
       const Pair rec = q0 == next_q0 ? next : load_pair(l2 + q0 + lane, q0 + lane < nsg);

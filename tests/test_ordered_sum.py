@@ -64,6 +64,15 @@ def _cases():
     both = r.random(1 << 18, dtype=F)
     both[7777], both[200000] = np.inf, -np.inf
     out["inf_then_neg_inf"] = both
+    # a sum that turns infinite early in a long chain: the walk skips to the
+    # blocks that can still change it (here a NaN, and an opposite infinity)
+    long_inf = r.random((1 << 22) + 9, dtype=F)
+    long_inf[10] = np.inf
+    out["inf_early_long"] = long_inf.copy()
+    long_inf[3_000_001] = np.nan
+    out["inf_early_then_nan_long"] = long_inf.copy()
+    long_inf[3_000_001] = -np.inf
+    out["inf_early_then_neg_inf_long"] = long_inf
     return out
 
 
