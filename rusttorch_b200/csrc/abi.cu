@@ -385,6 +385,7 @@ extern "C" rtc_result rtc_softmax(const rtc_tensor* x, size_t dim, const rtc_ten
   if (x->numel == 0) return ok();
   size_t outer, len, inner;
   split_dims(x, dim, &outer, &len, &inner);
+  const bool last = dim + 1 == x->ndim;     // ndarray's minimum-stride axis
   if (on_host(x)) {
     // Units are outer slices ([len, inner] each): every lane stays whole.
     const size_t ub = len * inner * sizeof(float);
@@ -395,13 +396,14 @@ extern "C" rtc_result rtc_softmax(const rtc_tensor* x, size_t dim, const rtc_ten
                                [=](const void* const* din, void* const* dout, size_t, size_t cu,
                                    cudaStream_t s) {
                                  return launch_softmax((const float*)din[0], cu, len, inner,
-                                                       (float*)dout[0], s);
+                                                       last, (float*)dout[0], s);
                                }),
                     "softmax");
   }
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
-  return launched(launch_softmax(cf(x), outer, len, inner, f(out), thread_stream()), "softmax");
+  return launched(launch_softmax(cf(x), outer, len, inner, last, f(out), thread_stream()),
+                  "softmax");
 }
 
 // ---------------------------------------------------------- dim reductions
@@ -414,6 +416,7 @@ static rtc_result reduce_dim(DimReduce op, const rtc_tensor* x, size_t dim, cons
   if (dim >= x->ndim) return invalid_dimension(context, dim, x->ndim - 1);
   size_t outer, len, inner;
   split_dims(x, dim, &outer, &len, &inner);
+  const bool last = dim + 1 == x->ndim;     // ndarray's minimum-stride axis
   if (op != kDimSum && len == 0) return empty_tensor(context);
   if (out->numel != outer * inner || out->dtype != x->dtype)
     return shape_mismatch_vec(std::string(context) + " (output)", reduced_shape(x, dim),
@@ -429,13 +432,13 @@ static rtc_result reduce_dim(DimReduce op, const rtc_tensor* x, size_t dim, cons
                                [=](const void* const* din, void* const* dout, size_t, size_t cu,
                                    cudaStream_t s) {
                                  return launch_reduce_dim(op, (const float*)din[0], cu, len,
-                                                          inner, (float*)dout[0], s);
+                                                          inner, last, (float*)dout[0], s);
                                }),
                     context);
   }
   DeviceScope scope(x->device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
-  return launched(launch_reduce_dim(op, cf(x), outer, len, inner, f(out), thread_stream()),
+  return launched(launch_reduce_dim(op, cf(x), outer, len, inner, last, f(out), thread_stream()),
                   context);
 }
 

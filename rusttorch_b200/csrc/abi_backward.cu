@@ -283,7 +283,7 @@ static rtc_result reduce_to_shape(const rtc_tensor* g, const rtc_tensor* o, cuda
   if (g->ndim == 2 && o->ndim == 2) {
     const size_t R = g->shape[0], C = g->shape[1];
     if (o->shape[0] == 1 && o->shape[1] == C)
-      return launched(launch_reduce_dim(kDimSum, x, 1, R, C, out, s), ctx);
+      return launched(launch_reduce_dim(kDimSum, x, 1, R, C, false, out, s), ctx);
     if (o->shape[1] == 1 && o->shape[0] == R)
       return launched(launch_lane_chain_sum(x, R, C, out, s), ctx);
   }
@@ -296,7 +296,7 @@ static rtc_result reduce_to_shape(const rtc_tensor* g, const rtc_tensor* o, cuda
   } else if (m == 1) {
     e = launch_lane_chain_sum(x, 1, blocks, out, s);
   } else {
-    e = launch_reduce_dim(kDimSum, x, 1, blocks, m, out, s);
+    e = launch_reduce_dim(kDimSum, x, 1, blocks, m, false, out, s);
   }
   // the ragged last block: out[j] += grad[blocks*m + j] for j < rem
   if (e == cudaSuccess && rem)

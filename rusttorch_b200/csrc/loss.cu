@@ -78,6 +78,8 @@ cudaError_t launch_terms(const osum::Plan& plan, const float* p, const float* t,
 
 size_t loss_scratch_bytes(LossOp op, size_t n) { return osum::scratch_bytes(n, loss_chains(op)); }
 
+size_t ordered_sum_scratch_bytes(size_t n, int chains) { return osum::scratch_bytes(n, chains); }
+
 cudaError_t launch_loss(LossOp op, const float* p, const float* t, size_t n, float a, float b,
                         void* scratch, float* sum_out, cudaStream_t s) {
   if (n == 0) return cudaSuccess;

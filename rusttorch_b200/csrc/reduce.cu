@@ -10,19 +10,25 @@
 // host repairs exactly those cases with one more scan (launch_index_scan).
 //
 // Dim reductions (reduction.rs:75-150, plus max along a dim), on a
-// C-contiguous tensor viewed as [outer, len, inner]:
-//  * inner == 1 (the reduced axis is the last one): ndarray reduces each lane
-//    with numeric_util::unrolled_fold — eight strided partial sums combined as
+// C-contiguous tensor viewed as [outer, len, inner].  ndarray's sum_axis
+// reduces lane by lane only along the minimum-stride axis; for the default
+// strides of a tensor built from a shape (IxDyn, all lengths > 0) that is the
+// LAST axis, because the axes after it have stride 1 as well when they have
+// length 1 and the reversed min_by_key keeps the last of equal strides.
+//  * the last axis (inner == 1): ndarray reduces each lane with
+//    numeric_util::unrolled_fold — eight strided partial sums combined as
 //    0+(p0+p4), +(p1+p5), +(p2+p6), +(p3+p7), then the tail.  Eight threads
 //    run the eight chains of one lane, each strictly sequential, so the result
 //    is ndarray's bit for bit.  Max uses a warp per lane (order-independent
 //    fmaxf) and re-folds a lane sequentially in the rare NaN/zero case.
-//  * inner > 1: ndarray accumulates `res = res + row` in row order, i.e. each
-//    output is a sequential chain over len.  One thread owns one output
-//    column; a CTA owns a strip of W columns and streams the rows through a
-//    multi-stage cp.async ring in shared memory, so HBM sees fully coalesced
-//    16-byte reads with ~150 KB in flight per SM while every column is still
-//    summed in row order (bit-exact).
+//  * any other axis: ndarray accumulates `res = res + row` in row order, i.e.
+//    each output is a sequential chain over len.  With inner > 1 one thread
+//    owns one output column; a CTA owns a strip of W columns and streams the
+//    rows through a multi-stage cp.async ring in shared memory, so HBM sees
+//    fully coalesced 16-byte reads with ~150 KB in flight per SM while every
+//    column is still summed in row order (bit-exact).  With inner == 1 (only
+//    length-1 axes follow `dim`) the lanes are contiguous but still one
+//    chain each: launch_lane_chain_sum.
 #include "rt_internal.h"
 #include "rt_fold.cuh"
 #include "rt_ops.cuh"
@@ -473,7 +479,9 @@ lane_sum8_staged_kernel(const float* x, size_t lanes, size_t len, float* out, in
 
 // ------------------------------------------------ last-axis sum, one chain
 // Each lane summed as ONE sequential f32 chain from 0.0, x[0] + x[1] + ...
-// in order (autograd's reduce_to_shape row sums, autograd/ops.rs:650-656).
+// in order (autograd's reduce_to_shape row sums, autograd/ops.rs:650-656;
+// ndarray's sum_axis over a non-last axis whose later axes all have length 1,
+// reduction.rs:86, activation.rs:127).
 // A CTA owns kLcRows lanes whose columns stream through a cp.async ring
 // kLcCols at a time; thread r of the first warp runs lane r's chain out of
 // shared memory.  Rows are padded to 68 floats so the chain threads' 16-byte
@@ -486,7 +494,7 @@ constexpr int kLcThreads = 64;
 constexpr int kLcSlots = kLcRows * (kLcCols / 4) / kLcThreads;   // 4 chunks per thread
 
 __global__ void __launch_bounds__(kLcThreads)
-lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
+lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out, bool mean) {
   __shared__ __align__(16) float smem[kLcStages][kLcRows][kLcPitch];
   const size_t lane0 = (size_t)blockIdx.x * kLcRows;
   const int rows = (int)min((size_t)kLcRows, lanes - lane0);
@@ -543,7 +551,14 @@ lane_chain_sum_kernel(const float* x, size_t lanes, size_t len, float* out) {
     }
   }
   cp_async_wait<0>();
-  if (chain) out[lane0 + tid] = acc;
+  if (chain) out[lane0 + tid] = mean ? fdiv(acc, (float)len) : acc;
+}
+
+// out[i] /= (f32)len: the mean of lanes whose chains the ordered-sum kernels
+// summed.
+__global__ void div_by_len_kernel(float* out, size_t lanes, size_t len) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < lanes) out[i] = fdiv(out[i], (float)len);
 }
 
 // ------------------------------------------------ last-axis sum, 4 lanes per warp
@@ -705,9 +720,11 @@ cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStre
 }
 
 cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
-                              size_t inner, float* out, cudaStream_t s) {
+                              size_t inner, bool last_axis, float* out, cudaStream_t s) {
   const size_t lanes = outer * inner;
   if (lanes == 0) return cudaSuccess;
+  if (inner == 1 && !last_axis && op != kDimMax)
+    return launch_lane_chain_sum(x, lanes, len, out, s, op == kDimMean);
   if (inner == 1) {
     if (op == kDimMax) {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
@@ -781,21 +798,40 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
 }
 
 cudaError_t launch_lane_chain_sum(const float* x, size_t lanes, size_t len, float* out,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, bool mean) {
   if (lanes == 0) return cudaSuccess;
+  if (len >= (size_t{1} << 18) && lanes <= (len >> 16)) {
+    // Few long lanes: one thread per chain would take len dependent adds
+    // (~2.6 ns each); the ordered-sum kernels reproduce the same chain with
+    // every SM working on one lane at a time.
+    const size_t bytes = ordered_sum_scratch_bytes(len, 1);
+    void* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(&scratch, bytes, s);
+    if (e != cudaSuccess) return e;
+    for (size_t l = 0; l < lanes && e == cudaSuccess; l++)
+      e = launch_ordered_sum_of(x + l * len, len, 1, 0.0f, scratch, out + l, s);
+    if (e == cudaSuccess && mean)
+      div_by_len_kernel<<<(unsigned)((lanes + 255) / 256), 256, 0, s>>>(out, lanes, len);
+    const cudaError_t ef = cudaFreeAsync(scratch, s);
+    if (e == cudaSuccess) e = ef;
+    return e == cudaSuccess ? cudaGetLastError() : e;
+  }
   if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0) {
     const size_t grid = (lanes + kLcRows - 1) / kLcRows;
     for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
       const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
       lane_chain_sum_kernel<<<(unsigned)ng, kLcThreads, 0, s>>>(
-          x + g0 * kLcRows * len, lanes - g0 * kLcRows, len, out + g0 * kLcRows);
+          x + g0 * kLcRows * len, lanes - g0 * kLcRows, len, out + g0 * kLcRows, mean);
     }
     return cudaGetLastError();
   }
-  // lane_generic_kernel<kDimSum> is the same chain, one thread per lane
+  // lane_generic_kernel is the same chain, one thread per lane
   const unsigned grid = (unsigned)std::max<size_t>(
       1, std::min<size_t>((lanes + kThreads - 1) / kThreads, (size_t)sm_count(cur_device()) * 8));
-  lane_generic_kernel<kDimSum><<<grid, kThreads, 0, s>>>(x, lanes, len, 1, out);
+  if (mean)
+    lane_generic_kernel<kDimMean><<<grid, kThreads, 0, s>>>(x, lanes, len, 1, out);
+  else
+    lane_generic_kernel<kDimSum><<<grid, kThreads, 0, s>>>(x, lanes, len, 1, out);
   return cudaGetLastError();
 }
 

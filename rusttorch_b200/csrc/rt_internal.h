@@ -100,9 +100,13 @@ cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStre
 
 enum DimReduce { kDimSum, kDimMean, kDimMax };
 // Reduce the middle axis of a C-contiguous [outer, len, inner] tensor.
-// inner == 1 is the contiguous-lane (last axis) case.
+// `last_axis`: the reduced axis is the tensor's last axis, which ndarray's
+// sum_axis reduces lane by lane with the eight-chain unrolled_fold (its
+// minimum-stride axis; default strides make that the last axis even when the
+// axes after `dim` all have length 1).  Any other axis is summed as one
+// row-order chain per output from 0.0 — with inner == 1 too.
 cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t len,
-                              size_t inner, float* out, cudaStream_t s);
+                              size_t inner, bool last_axis, float* out, cudaStream_t s);
 // The TMA-staged variant for inner > 1 (strip_tma.cu).  Sets *used = false
 // (and launches nothing) when the layout does not suit TMA.
 cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t len,
@@ -126,9 +130,9 @@ cudaError_t launch_gelu_autograd(const float* x, float* out, size_t n, cudaStrea
 cudaError_t launch_fill_from(const float* g, float* out, size_t n, double divisor, bool divide,
                              cudaStream_t s);
 // Each contiguous lane of length len summed as one sequential f32 chain from
-// 0.0, in element order.
+// 0.0, in element order; with `mean`, the chain's value / (f32)len.
 cudaError_t launch_lane_chain_sum(const float* x, size_t lanes, size_t len, float* out,
-                                  cudaStream_t s);
+                                  cudaStream_t s, bool mean = false);
 // sqrt(2/pi) as the reference computes it in f32.
 float gelu_k();
 
@@ -146,10 +150,13 @@ cudaError_t launch_loss(LossOp op, const float* p, const float* t, size_t n, flo
 // loss of the same chain count.
 cudaError_t launch_ordered_sum_of(const float* x, size_t n, int chains, float init, void* scratch,
                                   float* sum_out, cudaStream_t s);
+// Bytes of scratch launch_ordered_sum_of needs for n terms in `chains` chains.
+size_t ordered_sum_scratch_bytes(size_t n, int chains);
 
 // -------------------------------------------------------------------- softmax
-cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
-                           cudaStream_t s);
+// last_axis as for launch_reduce_dim: it picks the order of the sum of exps.
+cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner,
+                           bool last_axis, float* out, cudaStream_t s);
 
 // ------------------------------------------------------------------ generator
 cudaError_t launch_fill(float* out, size_t n, uint64_t seed, uint64_t offset, float a, float b,

@@ -4,7 +4,9 @@
 //   m = max_by fold (NaN compares Equal), e = exp(x - m), s = sum_axis(e),
 //   y = e / s
 // with ndarray's sum_axis order: the eight-chain unrolled_fold when dim is the
-// last axis, a sequential row-order chain otherwise.
+// last axis, a sequential row-order chain otherwise — also when every axis
+// after dim has length 1 (the lanes are then contiguous, but ndarray's
+// minimum-stride axis is still the last one).
 //
 // Every exponent is x - m <= 0 (or NaN), so the exponential is
 // expf_glibc_nonpos, which skips expf's overflow branches.
@@ -276,10 +278,14 @@ softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, floa
 
 }  // namespace
 
-cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner, float* out,
-                           cudaStream_t s) {
+cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner,
+                           bool last_axis, float* out, cudaStream_t s) {
   if (outer == 0 || len == 0 || inner == 0) return cudaSuccess;
-  if (inner > 1) {
+  // A non-last axis followed only by length-1 axes has contiguous lanes but
+  // ndarray's row-order chain for the sum: short lanes take the lane kernel,
+  // long ones the four-pass row path with that chain.
+  const bool chain = !last_axis;
+  if (inner > 1 || (chain && len < 2048)) {
     int dev = 0;
     cudaGetDevice(&dev);
     const size_t lanes = outer * inner;
@@ -290,13 +296,13 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
   }
   const size_t rows = outer;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
-  if (aligned && len % 4 == 0) {
+  if (!chain && aligned && len % 4 == 0) {
     if (len <= 512 * 2) return launch_row_reg<2>(x, rows, len, out, s);
     if (len <= 512 * 4) return launch_row_reg<4>(x, rows, len, out, s);
     if (len <= 512 * 8) return launch_row_reg<8>(x, rows, len, out, s);
     if (len <= 512 * 16) return launch_row_reg<16>(x, rows, len, out, s);
   }
-  if (len <= kMaxSmemRow) {
+  if (!chain && len <= kMaxSmemRow) {
     const size_t smem = len * sizeof(float);
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(softmax_row_kernel,
@@ -317,18 +323,21 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
   float* m = scratch;
   float* sm = scratch + rows;
   const unsigned gx = (unsigned)std::min<size_t>((len + kRowThreads - 1) / kRowThreads, 4096);
-  for (size_t r0 = 0; r0 < rows; r0 += 65535) {
+  for (size_t r0 = 0; r0 < rows && e == cudaSuccess; r0 += 65535) {
     const unsigned nr = (unsigned)std::min<size_t>(rows - r0, 65535);
     const float* xr = x + r0 * len;
     float* yr = out + r0 * len;
     row_max_kernel<<<nr, kRowThreads, 0, s>>>(xr, len, m + r0);
     row_exp_kernel<<<dim3(gx, nr), kRowThreads, 0, s>>>(xr, len, m + r0, yr);
-    row_chain_sum_kernel<<<nr, 32, 0, s>>>(yr, len, sm + r0);
+    if (chain)
+      e = launch_lane_chain_sum(yr, nr, len, sm + r0, s);
+    else
+      row_chain_sum_kernel<<<nr, 32, 0, s>>>(yr, len, sm + r0);
     row_div_kernel<<<dim3(gx, nr), kRowThreads, 0, s>>>(yr, len, sm + r0);
   }
-  e = cudaGetLastError();
-  cudaFreeAsync(scratch, s);
-  return e;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  const cudaError_t ef = cudaFreeAsync(scratch, s);
+  return e == cudaSuccess ? ef : e;
 }
 
 }  // namespace rt

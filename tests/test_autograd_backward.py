@@ -122,6 +122,7 @@ def test_oracle_backward_matches_numpy_restatement():
 @pytest.mark.parametrize("gshape,oshape", [
     ((5, 7), (1, 7)), ((5, 7), (5, 1)), ((5, 7), (7,)), ((5, 7), (35,)), ((2, 3, 4), (4,)),
     ((2, 3, 4), (2, 1, 4)), ((6,), (1,)), ((3, 4), (3, 4)), ((7,), (3,)), ((2, 2), (5,)),
+    ((9, 1), (1, 1)),
 ])
 def test_oracle_reduce_to_shape_matches_python(gshape, oshape):
     grad = O.normal(int(np.prod(gshape)), 21).reshape(gshape)
@@ -289,6 +290,10 @@ BA_CASES = [
     ((2048, 4096), (2048, 1), (2048, 4096)),
     ((300, 33), (300, 1), (300, 33)),       # rows of 33: the unaligned chain
     ((1000, 37), (1, 37), (1000, 37)),
+    ((19236, 1), (1, 1), (19236, 1)),       # [1, C] column sums with C == 1: one chain
+    ((1, 1), (99, 1), (99, 1)),
+    ((1 << 19, 1), (1, 1), (1 << 19, 1)),   # a long single column: the ordered-sum kernels
+    ((1,), (1 << 19,), (1 << 19,)),         # one chain over all, long
 ]
 
 

@@ -235,6 +235,27 @@ def test_golden_reductions():
                                           bits(GOLD[f"{op}_dim{dim}"]), err_msg=f"{op}_dim{dim}")
 
 
+def test_oracle_sum_axis_order_before_trailing_unit_axes():
+    # ndarray 0.15 sum_axis folds lanes with unrolled_fold only along the
+    # minimum-stride axis: min_by_key over the axes in reverse keeps the LAST
+    # axis of equal |stride|, and a length-1 axis after `dim` has stride 1 in
+    # the default strides, so [n, 1] summed over dim 0 is the row-order chain
+    # 0 + x0 + x1 + ..., not the eight-chain lane fold.
+    x = O.normal(4099, 65, 0, 3)
+    chain = np.float32(0.0)
+    for v in x:
+        chain = np.float32(chain + v)
+    lane = O.unrolled_sum_f32(x)
+    assert bits(chain) != bits(lane)          # the two orders differ on this input
+    for shape, dim in (((4099, 1), 0), ((1, 4099, 1, 1), 1)):
+        got = O.reduce_dim("sum", x.reshape(shape), dim).ravel()[0]
+        assert bits(got) == bits(chain), shape
+    assert bits(O.reduce_dim("sum", x.reshape(1, 4099), 1)[0]) == bits(lane)
+    s = O.softmax(x.reshape(4099, 1), 0).ravel()
+    e = np.exp(x.astype(np.float64) - x.max()).astype(np.float32)
+    assert abs(float(s.sum()) - 1.0) < 1e-4 and np.allclose(s, e / e.sum(), rtol=1e-5)
+
+
 def test_golden_softmax():
     d = ulp_diff(O.softmax(GOLD["m2"], 1), GOLD["softmax_dim1"])
     assert d.max() <= 4

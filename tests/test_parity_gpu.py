@@ -360,6 +360,31 @@ def test_last_axis_sum_row_kernels(shape, op):
     assert_bits_equal(got, O.reduce_dim(op, x, len(shape) - 1), f"{op}_dim {shape}")
 
 
+@pytest.mark.parametrize("shape,dim", [((4936, 1), 0), ((1512, 36, 57, 1), 2), ((83, 14, 1), 1),
+                                       ((6, 5515, 16, 1), 2), ((13605, 1, 22, 1), 2),
+                                       ((1 << 20, 1), 0), ((3, 1 << 19, 1, 1), 1),
+                                       ((40, 70000, 1), 1), ((5, 1), 0), ((7, 3, 1, 1), 0)])
+@pytest.mark.parametrize("op", ["sum", "mean", "max"])
+def test_dim_reduction_before_trailing_unit_axes(shape, dim, op):
+    """A non-last axis followed only by length-1 axes: the lanes are
+    contiguous, but ndarray's minimum-stride axis is still the last one, so
+    sum_axis adds each lane as one row-order chain from 0.0 (not the
+    eight-chain lane fold).  The long single lanes take the ordered-sum
+    kernels."""
+    x = O.normal(int(np.prod(shape)), 63, 0, 2).reshape(shape)
+    x.reshape(-1)[1] = -0.0
+    got = getattr(rt, f"{op}_dim")(dev(x), dim).to_numpy()
+    assert_bits_equal(got, O.reduce_dim(op, x, dim), f"{op}_dim {shape} dim={dim}")
+
+
+@pytest.mark.parametrize("shape,dim", [((1512, 36, 57, 1), 2), ((4936, 1), 0), ((59, 96, 1), 1),
+                                       ((50000, 1), 0), ((4, 3000, 1), 1), ((3, 1 << 19, 1), 1)])
+def test_softmax_before_trailing_unit_axes(shape, dim):
+    x = (O.normal(int(np.prod(shape)), 64, 0, 3)).reshape(shape)
+    got = rt.softmax(dev(x), dim).to_numpy()
+    assert_bits_equal(got, O.softmax(x, dim), f"softmax {shape} dim={dim}")
+
+
 def test_max_dim_with_nan_and_zero_lanes():
     x = O.normal(6 * 40, 47).reshape(6, 40)
     x[0, 10] = np.nan
