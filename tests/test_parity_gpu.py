@@ -372,7 +372,8 @@ def test_last_axis_sum_row_kernels(shape, op):
 @pytest.mark.parametrize("shape,dim", [((4936, 1), 0), ((1512, 36, 57, 1), 2), ((83, 14, 1), 1),
                                        ((6, 5515, 16, 1), 2), ((13605, 1, 22, 1), 2),
                                        ((1 << 20, 1), 0), ((3, 1 << 19, 1, 1), 1),
-                                       ((40, 70000, 1), 1), ((5, 1), 0), ((7, 3, 1, 1), 0)])
+                                       ((40, 70000, 1), 1), ((5, 1), 0), ((7, 3, 1, 1), 0),
+                                       ((4, 1 << 18, 1), 1), ((5, 1 << 18, 1), 1)])
 @pytest.mark.parametrize("op", ["sum", "mean", "max"])
 def test_dim_reduction_before_trailing_unit_axes(shape, dim, op):
     """A non-last axis followed only by length-1 axes: the lanes are
@@ -387,8 +388,11 @@ def test_dim_reduction_before_trailing_unit_axes(shape, dim, op):
 
 
 @pytest.mark.parametrize("shape,dim", [((1512, 36, 57, 1), 2), ((4936, 1), 0), ((59, 96, 1), 1),
-                                       ((50000, 1), 0), ((4, 3000, 1), 1), ((3, 1 << 19, 1), 1)])
+                                       ((50000, 1), 0), ((4, 3000, 1), 1), ((3, 1 << 19, 1), 1),
+                                       ((65537, 2048, 1), 1)])
 def test_softmax_before_trailing_unit_axes(shape, dim):
+    # (65537, 2048, 1): the four-pass row path runs its rows in launches of
+    # 65535; the last one holds two rows
     x = (O.normal(int(np.prod(shape)), 64, 0, 3)).reshape(shape)
     got = rt.softmax(dev(x), dim).to_numpy()
     assert_bits_equal(got, O.softmax(x, dim), f"softmax {shape} dim={dim}")
