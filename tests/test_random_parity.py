@@ -9,7 +9,8 @@ of a power of two after a large lead term), zeros of both signs, powers of
 two of mixed sign, half-integers, squares, with occasional NaN and +/-inf.
 The areas are the dim reductions, softmax, broadcasting binary ops with
 broadcast_add's backward fold, the losses, and the ordered f32 sums under
-the losses.
+the losses; a last group puts inputs and outputs off the 16-byte boundary and
+lets outputs alias inputs.
 """
 import ctypes
 import math
@@ -162,3 +163,59 @@ def test_random_ordered_sums(seed):
         N.check(N.lib().rtc_selftest_ordered_sum(t.desc, chains, init, ctypes.byref(v)))
         want = O.unrolled_sum_f32(x) if chains == 8 else O.chain_sum_f32(x, init)
         assert_bits_equal(np.float32(v.value), want, f"chains={chains} n={x.size}")
+
+
+def _view(x, off):
+    """x copied to the device `off` floats past the start of a fresh device
+    buffer (whose start is 256-byte aligned: off 1-3 is not 16-byte aligned)."""
+    import rusttorch_b200 as rt
+    from rusttorch_b200 import _native as N
+    n = x.size
+    base = rt.Tensor([n + off + 1])
+    h = np.zeros(n + off + 1, F)
+    h[off:off + n] = x.ravel()
+    N.check(N.lib().rtc_memcpy_h2d(0, ctypes.c_void_p(base.ptr), h.ctypes.data_as(ctypes.c_void_p),
+                                   h.nbytes))
+    return rt.Tensor.from_device_ptr(base.ptr + 4 * off, list(x.shape), owner=base)
+
+
+def _out_view(shape, off):
+    import rusttorch_b200 as rt
+    base = rt.Tensor([int(np.prod(shape)) + off + 1])
+    return rt.Tensor.from_device_ptr(base.ptr + 4 * off, list(shape), owner=base)
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_random_misaligned_views_and_in_place(seed):
+    """Inputs and outputs off the 16-byte boundary (the kernels' vector and
+    TMA paths give way to their scalar forms), outputs aliasing inputs."""
+    from rusttorch_b200 import _native as N
+    r = np.random.default_rng([6, seed])
+    shape = _shape(r, 1_000_000)
+    if r.random() < 0.3:
+        shape = shape + [1]
+    x = _values(r, int(np.prod(shape))).reshape(shape)
+    off = int(r.integers(1, 4))
+    vx = _view(x, off)
+    dim = int(r.integers(0, len(shape)))
+    oshape = [d for i, d in enumerate(shape) if i != dim]
+    for op in ("sum", "mean", "max"):
+        out = _out_view(oshape, int(r.integers(0, 4)))
+        N.check(getattr(N.lib(), f"rtc_{op}_dim")(vx.desc, dim, out.desc))
+        assert_bits_equal(out.to_numpy(), O.reduce_dim(op, x, dim), f"{op}_dim {shape} {dim}")
+    xs = (r.standard_normal(x.size) * 3).astype(F).reshape(shape)
+    vs = _view(xs, off)
+    N.check(N.lib().rtc_softmax(vs.desc, dim, vs.desc))          # in place
+    assert_bits_equal(vs.to_numpy(), O.softmax(xs, dim), f"softmax {shape} {dim}")
+    a, b = _values(r, x.size), _values(r, x.size)
+    va, vb = _view(a, off), _view(b, off)
+    N.check(N.lib().rtc_div(va.desc, vb.desc, va.desc))
+    assert_bits_equal(va.to_numpy(), O.binary("div", a, b), "div in place")
+    N.check(N.lib().rtc_gelu(vb.desc, vb.desc))
+    assert_bits_equal(vb.to_numpy(), O.unary("gelu", b), "gelu in place")
+    p = _values(r, x.size)
+    t = _values(r, x.size)
+    import rusttorch_b200 as rt
+    got = rt.mse_loss(_view(p, int(r.integers(0, 4))), _view(t, int(r.integers(0, 4))))
+    want = O.loss("mse", p, t)
+    assert (math.isnan(got) and math.isnan(want)) or got == want, (got, want)
