@@ -115,7 +115,13 @@ class Tensor:
 
     @property
     def desc(self):
-        return self._desc.ref
+        """A by-reference rtc_tensor for a C-ABI call.  It holds this tensor
+        (and so its device buffer) alive for as long as the reference itself
+        is alive, so `Tensor.from_numpy(a).desc` passed straight to a call is
+        safe: the temporary tensor is not freed before the call returns."""
+        s = _native.RtcTensor.from_buffer_copy(self._desc.s)
+        s._owner = self       # the copy -> the tensor; nothing points back
+        return ctypes.byref(s)
 
     def __del__(self):
         try:

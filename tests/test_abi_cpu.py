@@ -197,3 +197,22 @@ def test_sharded_stats_argument_checks_without_gpu():
     r = L.rtc_sharded_stats(None, 2, out)
     assert not r.success and r.code == N.INVALID_ARGUMENT
     L.rtc_free_error_message(r.error_msg)
+
+
+def test_tensor_desc_keeps_its_tensor_alive():
+    # A descriptor taken from a temporary tensor must not outlive its buffer:
+    # Tensor.desc holds the tensor until the by-reference struct is dropped.
+    import gc
+    import weakref
+
+    import rusttorch_b200 as rt
+    t = rt.Tensor([2, 3], ptr=0x1000)       # borrowed address: nothing to free
+    alive = weakref.ref(t)
+    ref = t.desc
+    del t
+    gc.collect()
+    assert alive() is not None
+    s = ref._obj
+    assert (s.ndim, s.numel, s.shape[0], s.shape[1], s.data) == (2, 6, 2, 3, 0x1000)
+    del ref, s
+    assert alive() is None                  # no cycle: freed without the collector
