@@ -140,3 +140,42 @@ extern "C" uint64_t act_max_ulp(int which, uint64_t start, uint64_t stop, uint64
 extern "C" void act_restated(int which, const float* x, float* out, uint64_t n) {
   for (uint64_t i = 0; i < n; i++) out[i] = act_mine(which, x[i]);
 }
+
+// Inputs u = start, start+stride, ... < stop where act_mine misses the
+// north_star tolerance for transcendental activations against act_ref: more
+// than 4 ulp AND more than 1e-6 relative error (NaN inputs skipped; two NaN
+// results are equal).  *first receives the first such input.
+extern "C" uint64_t act_tol_violations(int which, uint64_t start, uint64_t stop, uint64_t stride,
+                                       int threads, uint32_t* first) {
+  if (threads < 1) threads = 1;
+  std::vector<uint64_t> cnt(threads, 0), fst(threads, UINT64_MAX);
+  std::vector<std::thread> pool;
+  const uint64_t count = stop > start ? (stop - start + stride - 1) / stride : 0;
+  for (int t = 0; t < threads; t++) {
+    pool.emplace_back([&, t] {
+      const uint64_t lo = count * t / threads, hi = count * (t + 1) / threads;
+      for (uint64_t k = lo; k < hi; k++) {
+        const uint32_t u = (uint32_t)(start + k * stride);
+        float x;
+        memcpy(&x, &u, 4);
+        if (isnan(x)) continue;
+        const float a = act_ref(which, x), b = act_mine(which, x);
+        if (isnan(a) && isnan(b)) continue;
+        const int64_t d = ordered(a) - ordered(b);
+        if ((d < 0 ? -d : d) <= 4) continue;
+        const double rel = fabs((double)a - (double)b) / fabs((double)a);
+        if (rel <= 1e-6) continue;
+        if (fst[t] == UINT64_MAX) fst[t] = u;
+        cnt[t]++;
+      }
+    });
+  }
+  uint64_t c = 0, f = UINT64_MAX;
+  for (int t = 0; t < threads; t++) {
+    pool[t].join();
+    c += cnt[t];
+    if (fst[t] < f) f = fst[t];
+  }
+  if (first) *first = (uint32_t)(f == UINT64_MAX ? 0 : f);
+  return c;
+}

@@ -43,6 +43,9 @@ def load_check_lib():
     lib.act_max_ulp.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
                                 ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
                                 ctypes.POINTER(ctypes.c_uint32)]
+    lib.act_tol_violations.restype = ctypes.c_uint64
+    lib.act_tol_violations.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
+                                       ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
     lib.act_restated.restype = None
     lib.act_restated.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64]
     return lib
@@ -167,3 +170,16 @@ def test_softplus_and_mish_ulp_bounds(chk, which):
         for u in MISH_WORST:
             m = chk.act_max_ulp(1, u, u + 1, 1, 1, 4, ctypes.byref(over), ctypes.byref(worst))
             assert 4 < m <= 6, (hex(u), m)
+
+
+@pytest.mark.parametrize("which", [0, 1])
+def test_softplus_and_mish_within_the_stated_tolerance(chk, which):
+    # BASELINE's bar for transcendental activations: within 1e-6 relative
+    # error, or 4 ulp.  mish's 5-6 ulp inputs are normal floats near
+    # |x| = 0.1-0.35, where 6 ulp is below 7.2e-7 relative.
+    stride = 1 if os.environ.get("RT_EXHAUSTIVE") == "1" else 211
+    first = ctypes.c_uint32()
+    n = chk.act_tol_violations(which, 0, 1 << 32, stride, os.cpu_count() or 1, ctypes.byref(first))
+    assert n == 0, (which, n, hex(first.value))
+    for u in MISH_WORST:
+        assert chk.act_tol_violations(1, u, u + 1, 1, 1, ctypes.byref(first)) == 0, hex(u)
