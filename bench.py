@@ -1,21 +1,25 @@
 """Benchmark: HBM GB/s of rusttorch-core's hot path on B200 (BASELINE.json metric).
 
 One step = one pass of the four ops the metric names, each on its
-BASELINE.json config, per GPU (weak scaling: every rank owns one full-size
-shard of each tensor; shard r holds elements [r*n, (r+1)*n) of one seeded
-global stream):
+BASELINE.json config:
   add->mul_scalar  cfg1  2 x [2^24] U[-1,1)                 12 B/element
-  sum              cfg2  [2^28] N(0,1); N > 1: local exact   4 B/element
-                         summary + NCCL all-gather + rank-order combine
+  sum              cfg2  [2^28] N(0,1)                        4 B/element
   softmax(dim=1)   cfg4  [32768, 4096] N(0,2)                 8 B/element
   adamw (in place) cfg5  4 x [2^30], lr 1e-3, b (0.9, 0.999),
                          eps 1e-8, wd 0.01, t 10             28 B/element
-value = algorithmic bytes of all ranks / max-over-ranks device time.
+Strong scaling (default): on N GPUs rank r owns elements [r*n/N, (r+1)*n/N)
+of cfg1, cfg2 and cfg5 and rows [r*32768/N, (r+1)*32768/N) of cfg4, cut from
+the same seeded streams as the N = 1 tensors.  The sum's per-GPU f64
+partials are combined by an NCCL all-reduce, the only exchange; the other
+ops need none.  `--scaling weak` gives every GPU a full-size copy instead.
+value = algorithmic bytes of the whole step / max-over-ranks device time.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --suite [--only REGEX]     # every op alone, one GPU
+    python bench.py --probe [--only REGEX]     # read/copy ceilings, cfg1 sizing
 
-Prints ONE JSON line on rank 0.
+Prints ONE JSON line on rank 0 (one per op with --suite / --probe).
 """
 from __future__ import annotations
 
@@ -259,12 +263,50 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------- GPU arm
+def shard_of(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Rank r's contiguous share [lo, hi) of n units (rows or elements)."""
+    return n * rank // world, n * (rank + 1) // world
+
+
+class Layout:
+    """What one rank holds: under strong scaling its contiguous share of
+    every config (cfg1/cfg2/cfg5 by elements, cfg4 by rows of 4096); under
+    weak scaling a full-size shard of each (shard r = elements [r*n, (r+1)*n)
+    of the same seeded stream).  `off*` are the offsets of the rank's first
+    element in the global seeded stream, so the shards of all ranks together
+    are exactly the N = 1 tensors."""
+
+    def __init__(self, rank: int, world: int, scaling: str):
+        self.scaling = scaling
+        if scaling == "strong":
+            lo1, hi1 = shard_of(N1, rank, world)
+            lo2, hi2 = shard_of(N2, rank, world)
+            lo4, hi4 = shard_of(R4, rank, world)
+            lo5, hi5 = shard_of(N5, rank, world)
+            self.n1, self.off1 = hi1 - lo1, lo1
+            self.n2, self.off2 = hi2 - lo2, lo2
+            self.r4, self.off4 = hi4 - lo4, lo4 * C4
+            self.n5, self.off5 = hi5 - lo5, lo5
+        else:
+            self.n1, self.off1 = N1, rank * N1
+            self.n2, self.off2 = N2, rank * N2
+            self.r4, self.off4 = R4, rank * R4 * C4
+            self.n5, self.off5 = N5, rank * N5
+        self.bytes = {"add_mul_scalar": 12 * self.n1, "sum": 4 * self.n2,
+                      "softmax": 8 * self.r4 * C4, "adamw": 28 * self.n5}
+        self.elems = {"add_mul_scalar": self.n1, "sum": self.n2, "softmax": self.r4 * C4,
+                      "adamw": self.n5}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong (default): the BASELINE configs split over the N GPUs; weak: "
+                         "every GPU holds a full-size copy of each config")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops", default=",".join(OPS),
@@ -274,6 +316,8 @@ def main() -> None:
                          "prints one JSON line per op")
     ap.add_argument("--only", default="",
                     help="with --suite: time only the ops whose name matches this regex")
+    ap.add_argument("--configs", default="cfg1,cfg2,cfg3,cfg4,cfg5",
+                    help="with --suite: the configs to allocate and time (profiling)")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: sum 2^26, softmax 8192x4096, adamw 4x2^26 (all > L2)")
     args = ap.parse_args()
@@ -293,7 +337,6 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    import rusttorch_b200 as rt
     from rusttorch_b200 import _native as N
 
     rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
@@ -301,65 +344,79 @@ def main() -> None:
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    L = Layout(rank, world, args.scaling)
     lib = N.lib()
     stream = torch.cuda.current_stream()
     N.check(lib.rtc_set_stream(c_void_p(stream.cuda_stream)))
     ops = [o for o in args.ops.split(",") if o]
 
     def empty(n):
-        return torch.empty(n, dtype=torch.float32, device="cuda")
+        return torch.empty(max(n, 1), dtype=torch.float32, device="cuda")
 
     def desc(t, shape):
         return N.Desc(t.data_ptr(), shape, N.F32, local)
 
-    def fill(t, shape, seed, normal, a_, b_):
-        d = desc(t, shape)
-        n = t.numel()
+    def fill(t, shape, seed, normal, a_, b_, offset):
         fn = lib.rtc_fill_normal if normal else lib.rtc_fill_uniform
-        N.check(fn(d.ref, seed, rank * n, a_, b_))
+        N.check(fn(desc(t, shape).ref, seed, offset, a_, b_))
 
+    shape = {"a": [L.n1], "b": [L.n1], "c": [L.n1], "x2": [L.n2], "x4": [L.r4, C4],
+             "y4": [L.r4, C4], "p": [L.n5], "g": [L.n5], "m": [L.n5], "v": [L.n5]}
     bufs = {}
     if "add_mul_scalar" in ops:
-        bufs["a"], bufs["b"], bufs["c"] = empty(N1), empty(N1), empty(N1)
-        fill(bufs["a"], [N1], 1, False, -1.0, 1.0)
-        fill(bufs["b"], [N1], 101, False, -1.0, 1.0)
+        bufs["a"], bufs["b"], bufs["c"] = empty(L.n1), empty(L.n1), empty(L.n1)
+        fill(bufs["a"], [L.n1], 1, False, -1.0, 1.0, L.off1)
+        fill(bufs["b"], [L.n1], 101, False, -1.0, 1.0, L.off1)
     if "sum" in ops:
-        bufs["x2"] = empty(N2)
-        fill(bufs["x2"], [N2], 2, True, 0.0, 1.0)
+        bufs["x2"] = empty(L.n2)
+        fill(bufs["x2"], [L.n2], 2, True, 0.0, 1.0, L.off2)
     if "softmax" in ops:
-        bufs["x4"], bufs["y4"] = empty(R4 * C4), empty(R4 * C4)
-        fill(bufs["x4"], [R4, C4], 4, True, 0.0, 2.0)
+        bufs["x4"], bufs["y4"] = empty(L.r4 * C4), empty(L.r4 * C4)
+        fill(bufs["x4"], [L.r4, C4], 4, True, 0.0, 2.0, L.off4)
     if "adamw" in ops:
         for k, seed, normal, a_, b_ in (("p", 51, True, 0.0, 0.02), ("g", 52, True, 0.0, 1e-2),
                                         ("m", 53, True, 0.0, 1e-3), ("v", 54, False, 0.0, 1e-4)):
-            bufs[k] = empty(N5)
-            fill(bufs[k], [N5], seed, normal, a_, b_)
-    D = {}
-    if "add_mul_scalar" in ops:
-        D["a"], D["b"], D["c"] = (desc(bufs[k], [N1]) for k in "abc")
-    if "sum" in ops:
-        D["x2"] = desc(bufs["x2"], [N2])
-    if "softmax" in ops:
-        D["x4"], D["y4"] = desc(bufs["x4"], [R4, C4]), desc(bufs["y4"], [R4, C4])
-    if "adamw" in ops:
-        for k in "pgmv":
-            D[k] = desc(bufs[k], [N5])
+            bufs[k] = empty(L.n5)
+            fill(bufs[k], [L.n5], seed, normal, a_, b_, L.off5)
+    D = {k: desc(bufs[k], shape[k]) for k in bufs}
     torch.cuda.synchronize()
 
-    # The sum lands in device memory without a host round trip; at N > 1 the
-    # f64 partials are all-gathered over NCCL (the hot path's only exchange).
+    # Before timing (N > 1): the sharded sum/max/min of cfg2 through the
+    # exact per-shard summaries, all-gathered and folded in rank order,
+    # against the NCCL all-reduce of the f64 partials the timed step uses.
+    check = None
     sum_dev = torch.zeros(1, dtype=torch.float64, device="cuda")
-    sum_all = torch.zeros(world, dtype=torch.float64, device="cuda")
+    if world > 1 and "sum" in ops:
+        from rusttorch_b200 import sharded as sh
+        exact = sh.ShardedReducer(lib, rank, world).stats(D["x2"])
+        N.check(lib.rtc_sum_device(D["x2"].ref, c_void_p(sum_dev.data_ptr())))
+        dist.all_reduce(sum_dev)
+        got = float(sum_dev.item())
+        absx = torch.tensor([float(bufs["x2"].abs().double().sum())], dtype=torch.float64,
+                            device="cuda")
+        dist.all_reduce(absx)
+        tol = 1e-6 * float(absx.item())
+        if abs(got - exact[0]) > tol:
+            raise SystemExit(f"sharded sum mismatch: all-reduce {got!r} vs rank-order {exact[0]!r}")
+        check = {"sum": exact[0], "mean": exact[1], "max": exact[2], "min": exact[3],
+                 "allreduce_sum_minus_exact": got - exact[0], "tolerance": tol}
 
-    def run_op(op):
+    # The sum lands in device memory without a host round trip; at N > 1 the
+    # per-GPU f64 partials are combined by an NCCL all-reduce (the hot path's
+    # only exchange), timed on its own as well.
+    def run_op(op, coll_ev=None):
         if op == "add_mul_scalar":
             N.check(lib.rtc_add_mul_scalar(D["a"].ref, D["b"].ref, 0.5, D["c"].ref))
         elif op == "sum":
             N.check(lib.rtc_sum_device(D["x2"].ref, c_void_p(sum_dev.data_ptr())))
             if world > 1:
-                dist.all_gather_into_tensor(sum_all, sum_dev)
+                if coll_ev is not None:
+                    coll_ev[0].record(stream)
+                dist.all_reduce(sum_dev)
+                if coll_ev is not None:
+                    coll_ev[1].record(stream)
         elif op == "softmax":
             N.check(lib.rtc_softmax(D["x4"].ref, 1, D["y4"].ref))
         elif op == "adamw":
@@ -377,11 +434,14 @@ def main() -> None:
     torch.cuda.synchronize()
 
     # Events around every op of every step; the ops' inputs are re-read only
-    # a full step later, after >= 17 GB of other traffic, so L2 (126 MB) holds
-    # none of them when they start.
-    ev = {op: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)] for op in ops}
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # a full step later, after >= 3.7 GB of other traffic per GPU (N <= 8),
+    # so L2 (126 MB) holds none of them when they start.
+    def evpair():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    ev = {op: [evpair() for _ in range(args.steps)] for op in ops}
+    coll = [evpair() for _ in range(args.steps)]
+    start, stop = evpair()
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
@@ -390,43 +450,50 @@ def main() -> None:
             for op in ops:
                 e0, e1 = ev[op][k]
                 e0.record(stream)
-                run_op(op)
+                run_op(op, coll[k])
                 e1.record(stream)
         stop.record(stream)
         torch.cuda.synchronize()
     barrier()
     total_ms = start.elapsed_time(stop)
     op_ms = {op: sum(e0.elapsed_time(e1) for e0, e1 in ev[op]) / args.steps for op in ops}
+    coll_ms = (sum(e0.elapsed_time(e1) for e0, e1 in coll) / args.steps
+               if world > 1 and "sum" in ops else 0.0)
     if world > 1:
-        t = torch.tensor([total_ms] + [op_ms[o] for o in ops], dtype=torch.float64, device="cuda")
+        t = torch.tensor([total_ms, coll_ms] + [op_ms[o] for o in ops], dtype=torch.float64,
+                         device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t[0])
-        op_ms = {o: float(t[i + 1]) for i, o in enumerate(ops)}
+        total_ms, coll_ms = float(t[0]), float(t[1])
+        op_ms = {o: float(t[i + 2]) for i, o in enumerate(ops)}
     ms_step = total_ms / args.steps
-    step_bytes = sum(BYTES[o] for o in ops) * world
+    rank_bytes = sum(L.bytes[o] for o in ops)
+    step_bytes = rank_bytes * world if args.scaling == "weak" else sum(BYTES[o] for o in ops)
     value = step_bytes / (ms_step * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
-    per_op = {o: {"ms": op_ms[o], "GB_s": BYTES[o] / (op_ms[o] * 1e-3) / 1e9,
-                  "elements_per_s": ELEMS[o] / (op_ms[o] * 1e-3),
-                  "frac_of_measured_peak": BYTES[o] / (op_ms[o] * 1e-3) / 1e9 / peak,
-                  "frac_of_8TBs_spec": BYTES[o] / (op_ms[o] * 1e-3) / 1e9 / SPEC_HBM_GBS}
+    per_op = {o: {"ms": op_ms[o], "GB_s_per_gpu": L.bytes[o] / (op_ms[o] * 1e-3) / 1e9,
+                  "elements_per_s_per_gpu": L.elems[o] / (op_ms[o] * 1e-3),
+                  "frac_of_measured_peak": L.bytes[o] / (op_ms[o] * 1e-3) / 1e9 / peak,
+                  "frac_of_8TBs_spec": L.bytes[o] / (op_ms[o] * 1e-3) / 1e9 / SPEC_HBM_GBS}
               for o in ops}
+    if world > 1 and "sum" in ops:
+        per_op["sum"]["nccl_allreduce_ms"] = coll_ms
     dom = max(ops, key=lambda o: op_ms[o])
-    achieved = BYTES[dom] / (op_ms[dom] * 1e-3) / 1e9
+    achieved = L.bytes[dom] / (op_ms[dom] * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic_per_launch.txt"
     if tf.exists():
         for line in tf.read_text().splitlines():
             parts = line.split()
-            if len(parts) >= 2 and parts[0] == dom:
-                traffic = int(parts[1])
+            if len(parts) >= 3 and parts[0] == dom:
+                # bytes per element, from the ncu capture, times this launch's elements
+                traffic = int(round(float(parts[2]) * L.elems[dom]))
     gpu_launches = args.steps * sum({"add_mul_scalar": 1, "sum": 2, "softmax": 1,
                                      "adamw": 1}[o] for o in ops)
 
     # e2e: the same step through the C ABI from pinned host buffers.
     e2e = None
     if not args.no_e2e and set(ops) == set(OPS):
-        e2e = run_e2e(args, lib, N, torch, D, bufs, rank, world, stream)
+        e2e = run_e2e(args, lib, N, torch, L, bufs, shape, rank, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and set(ops) == set(OPS):
@@ -437,17 +504,23 @@ def main() -> None:
                    "sample": f"unavailable: {ex}"}
 
     if rank == 0:
+        split = ("cfg1/cfg2/cfg5 split into N contiguous element ranges, cfg4 into N row blocks"
+                 if args.scaling == "strong" else "every GPU holds a full-size copy of each config")
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic (seeded device generator, BASELINE.json shapes/distributions)",
             "config": {"workload": "add->mul_scalar cfg1 [2^24] + sum cfg2 [2^28] + softmax "
-                                   "cfg4 [32768,4096] dim 1 + adamw cfg5 4x[2^30] per GPU",
-                       "ops": ops, "per_gpu_bytes_per_step": step_bytes // world,
-                       "l2": "no flush: each op's inputs are re-read only after >= 17 GB of "
-                             "other traffic (L2 is 126 MB)",
-                       "parallelism": f"dp{world} (weak: one full shard per GPU)"},
+                                   "cfg4 [32768,4096] dim 1 + adamw cfg5 4x[2^30]"
+                                   + (" per GPU" if args.scaling == "weak" else
+                                      ", split over the GPUs"),
+                       "ops": ops, "step_bytes": step_bytes, "per_gpu_bytes_per_step": rank_bytes,
+                       "split": split,
+                       "l2": "no flush: each op's inputs are re-read only after >= 3.7 GB of "
+                             "other traffic per GPU (L2 is 126 MB)",
+                       "parallelism": f"dp{world} ({args.scaling})"},
             "frac_of_peak": value / (peak * world),
             "per_op": per_op,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
@@ -459,17 +532,21 @@ def main() -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        if check is not None:
+            line["sharded_check"] = check
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_e2e(args, lib, N, torch, D, bufs, rank, world, stream):
+def run_e2e(args, lib, N, torch, L, bufs, shape, rank, world):
     """The same step through the C ABI on tensors in pinned host memory
     (rtc_tensor.device = RTC_HOST_MEMORY): the library streams every op's
     inputs to the GPU and its results back (c, the sum, y, and p/m/v in
-    place), copies overlapped with the kernels.  Timed on the host clock
-    from the first input byte to the last result byte, max over ranks."""
+    place), copies overlapped with the kernels.  Each rank streams its own
+    shard through its own GPU; at N > 1 the sum's shard summaries are
+    all-gathered and folded in rank order.  Timed on the host clock from the
+    first input byte to the last result byte, max over ranks."""
     import torch.distributed as dist
 
     k_e2e = max(1, min(args.steps, 3))
@@ -479,8 +556,6 @@ def run_e2e(args, lib, N, torch, D, bufs, rank, world, stream):
         host[k] = torch.empty(bufs[k].numel(), dtype=torch.float32, pin_memory=True)
         host[k].copy_(bufs[k])
     torch.cuda.synchronize()
-    shape = {"a": [N1], "b": [N1], "c": [N1], "x2": [N2], "x4": [R4, C4], "y4": [R4, C4],
-             "p": [N5], "g": [N5], "m": [N5], "v": [N5]}
     H = {k: N.Desc(host[k].data_ptr(), shape[k], N.F32, HOST) for k in host}
     h2d = sum(host[k].numel() * 4 for k in ("a", "b", "x2", "x4", "p", "g", "m", "v"))
     d2h = sum(host[k].numel() * 4 for k in ("c", "y4", "p", "m", "v"))
@@ -512,16 +587,21 @@ def run_e2e(args, lib, N, torch, D, bufs, rank, world, stream):
         tt = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt[0])
-    value = sum(BYTES.values()) * world / (ms * 1e-3) / 1e9
+    total = sum(L.bytes.values()) * (world if L.scaling == "weak" else 1)
+    if L.scaling == "strong":
+        total = sum(BYTES.values())
+    value = total / (ms * 1e-3) / 1e9
     return {"value": value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "steps": k_e2e,
             "path": "C-ABI ops on pinned host tensors (device = RTC_HOST_MEMORY): chunked H2D, "
-                    "kernel and D2H overlapped on three streams inside the library"}
+                    "kernel and D2H overlapped on three streams inside the library; each rank "
+                    "streams its own shard"}
 
 
 def run_suite(args) -> None:
     """Every op of every BASELINE.json config, timed alone on one GPU: CUDA
-    events around each call, L2 flushed (256 MiB written) before each one,
+    events around each call, L2 flushed (256 MiB written, 256 MiB read)
+    before each one,
     median of max(3, --steps) runs.  One JSON line per op."""
     import torch
 
@@ -532,7 +612,12 @@ def run_suite(args) -> None:
     stream = torch.cuda.current_stream()
     N.check(lib.rtc_set_stream(c_void_p(stream.cuda_stream)))
     peak, _ = peak_hbm()
+    # L2 flush before each run: 256 MiB written, then another 256 MiB read,
+    # so the run starts with no line of its inputs in L2 and no dirty line
+    # left to write back (the write alone would leave an L2 of dirty lines
+    # for the timed kernel to evict: 7 % of a 201 MB op, see --probe).
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 
     def t(shape):
         n = 1
@@ -555,6 +640,7 @@ def run_suite(args) -> None:
         times = []
         for _ in range(max(3, args.steps)):
             flush.zero_()
+            flush_rd.sum()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             fn()
@@ -574,109 +660,206 @@ def run_suite(args) -> None:
         print(json.dumps(row), flush=True)
 
     lr, b1, b2, eps, wd, tt = ADAMW
-    # cfg1
-    a, b, c = t([N1]), t([N1]), t([N1])
-    fill(a, 1)
-    fill(b, 101)
-    for name, fn in (("add", lib.rtc_add), ("sub", lib.rtc_sub), ("mul", lib.rtc_mul),
-                     ("div", lib.rtc_div)):
-        timeit(name, f"cfg1 [{N1}]", 12 * N1,
-               lambda fn=fn: N.check(fn(a[1].ref, b[1].ref, c[1].ref)))
-    timeit("mul_scalar", f"cfg1 [{N1}]", 8 * N1,
-           lambda: N.check(lib.rtc_mul_scalar(a[1].ref, 0.5, c[1].ref)))
-    timeit("add->mul_scalar (fused)", f"cfg1 [{N1}]", 12 * N1,
-           lambda: N.check(lib.rtc_add_mul_scalar(a[1].ref, b[1].ref, 0.5, c[1].ref)))
-    timeit("add then mul_scalar (two kernels)", f"cfg1 [{N1}]", 20 * N1,
-           lambda: (N.check(lib.rtc_add(a[1].ref, b[1].ref, c[1].ref)),
-                    N.check(lib.rtc_mul_scalar(c[1].ref, 0.5, c[1].ref))))
-    # losses (ops/loss.rs) on cfg1's shape: predictions uniform in [0, 1);
-    # targets uniform in [-1, 1) for the regression losses and in [0, 1) (soft
-    # labels, the cross-entropies' domain) for bce/ce
-    v1 = c_double()
-    fill(c, 102, False, 0.0, 1.0)
-    fill(b, 103, False, 0.0, 1.0)
-    for name, fn, extra, tg in (("mse_loss", lib.rtc_mse_loss, (), a),
-                                ("l1_loss", lib.rtc_l1_loss, (), a),
-                                ("smooth_l1_loss", lib.rtc_smooth_l1_loss, (1.0,), a),
-                                ("binary_cross_entropy_loss", lib.rtc_binary_cross_entropy_loss,
-                                 (1e-7,), b),
-                                ("cross_entropy_loss", lib.rtc_cross_entropy_loss, (1e-7,), b)):
-        timeit(name, f"cfg1 [{N1}]", 8 * N1,
-               lambda fn=fn, extra=extra, tg=tg: N.check(fn(c[1].ref, tg[1].ref, *extra,
-                                                            byref(v1))))
-    del a, b, c
-    # cfg2
-    x = t([N2])
-    fill(x, 2, True, 0.0, 1.0)
-    sd = torch.zeros(1, dtype=torch.float64, device="cuda")
-    v = c_double()
-    timeit("sum (device result)", f"cfg2 [{N2}]", 4 * N2,
-           lambda: N.check(lib.rtc_sum_device(x[1].ref, c_void_p(sd.data_ptr()))))
-    for name, fn in (("sum", lib.rtc_sum), ("mean", lib.rtc_mean), ("max", lib.rtc_max),
-                     ("min", lib.rtc_min)):
-        timeit(name + " (host result)", f"cfg2 [{N2}]", 4 * N2,
-               lambda fn=fn: N.check(fn(x[1].ref, byref(v))))
-    st4 = (c_double * 4)()
-    timeit("stats: sum+mean+max+min, one pass (host result)", f"cfg2 [{N2}]", 4 * N2,
-           lambda: N.check(lib.rtc_stats(x[1].ref, st4)))
-    del x
-    # cfg3
-    x = t([R3, C3])
-    fill(x, 3)
-    for dim, outn in ((1, R3), (0, C3)):
-        o = t([outn])
-        for name, fn in (("sum_dim", lib.rtc_sum_dim), ("mean_dim", lib.rtc_mean_dim),
-                         ("max_dim", lib.rtc_max_dim)):
-            timeit(f"{name}({dim})", f"cfg3 [{R3},{C3}]", 4 * R3 * C3 + 4 * outn,
-                   lambda fn=fn, o=o, dim=dim: N.check(fn(x[1].ref, dim, o[1].ref)))
-    del x
-    # cfg4
-    x, y = t([R4, C4]), t([R4, C4])
-    fill(x, 4, True, 0.0, 2.0)
-    for name in ("relu", "gelu", "swish", "sigmoid", "tanh", "selu", "softsign", "mish",
-                 "softplus"):
-        fn = getattr(lib, "rtc_" + name)
-        timeit(name, f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
-               lambda fn=fn: N.check(fn(x[1].ref, y[1].ref)))
-    timeit("leaky_relu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
-           lambda: N.check(lib.rtc_leaky_relu(x[1].ref, y[1].ref, 0.01)))
-    timeit("elu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
-           lambda: N.check(lib.rtc_elu(x[1].ref, y[1].ref, 1.0)))
-    timeit("softmax(1)", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
-           lambda: N.check(lib.rtc_softmax(x[1].ref, 1, y[1].ref)))
-    bias = t([C4])
-    fill(bias, 9)
-    timeit("add_broadcast (row bias)", f"cfg4 [{R4},{C4}] + [{C4}]", 8 * R4 * C4 + 4 * C4,
-           lambda: N.check(lib.rtc_add_broadcast(x[1].ref, bias[1].ref, y[1].ref)))
-    # autograd backward (autograd/ops.rs) on cfg4's shape
-    g, z, w = t([R4, C4]), t([R4, C4]), t([R4, C4])
-    fill(g, 10, True, 0.0, 1.0)
-    fill(z, 11, True, 1.0, 0.5)
-    for name in ("relu", "sigmoid", "tanh", "gelu"):
-        fn = getattr(lib, f"rtc_{name}_backward")
-        timeit(f"{name}_backward", f"cfg4 [{R4},{C4}]", 12 * R4 * C4,
-               lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, y[1].ref)))
-    for name in ("mul", "div"):
-        fn = getattr(lib, f"rtc_{name}_backward")
-        timeit(f"{name}_backward (both grads)", f"cfg4 [{R4},{C4}]", 20 * R4 * C4,
-               lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, z[1].ref, y[1].ref, w[1].ref)))
-    cols, rows = t([1, C4]), t([R4, 1])
-    timeit("broadcast_add_backward -> [1,C]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * C4,
-           lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, cols[1].ref, None)))
-    timeit("broadcast_add_backward -> [R,1]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * R4,
-           lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, rows[1].ref, None)))
-    del x, y, g, z, w
-    # cfg5
-    P = {k: t([N5]) for k in "pgmv"}
-    fill(P["p"], 51, True, 0.0, 0.02)
-    fill(P["g"], 52, True, 0.0, 1e-2)
-    fill(P["m"], 53, True, 0.0, 1e-3)
-    fill(P["v"], 54, False, 0.0, 1e-4)
-    timeit("adamw (in place)", f"cfg5 4x[{N5}]", 28 * N5,
-           lambda: N.check(lib.rtc_adamw_update(P["p"][1].ref, P["g"][1].ref, P["m"][1].ref,
-                                                P["v"][1].ref, lr, b1, b2, eps, wd, tt,
-                                                P["p"][1].ref, P["m"][1].ref, P["v"][1].ref)))
+    cfgs = set(args.configs.split(","))
+    if "cfg1" in cfgs:   # cfg1
+        a, b, c = t([N1]), t([N1]), t([N1])
+        fill(a, 1)
+        fill(b, 101)
+        for name, fn in (("add", lib.rtc_add), ("sub", lib.rtc_sub), ("mul", lib.rtc_mul),
+                         ("div", lib.rtc_div)):
+            timeit(name, f"cfg1 [{N1}]", 12 * N1,
+                   lambda fn=fn: N.check(fn(a[1].ref, b[1].ref, c[1].ref)))
+        timeit("mul_scalar", f"cfg1 [{N1}]", 8 * N1,
+               lambda: N.check(lib.rtc_mul_scalar(a[1].ref, 0.5, c[1].ref)))
+        timeit("add->mul_scalar (fused)", f"cfg1 [{N1}]", 12 * N1,
+               lambda: N.check(lib.rtc_add_mul_scalar(a[1].ref, b[1].ref, 0.5, c[1].ref)))
+        timeit("add then mul_scalar (two kernels)", f"cfg1 [{N1}]", 20 * N1,
+               lambda: (N.check(lib.rtc_add(a[1].ref, b[1].ref, c[1].ref)),
+                        N.check(lib.rtc_mul_scalar(c[1].ref, 0.5, c[1].ref))))
+        # losses (ops/loss.rs) on cfg1's shape: predictions uniform in [0, 1);
+        # targets uniform in [-1, 1) for the regression losses and in [0, 1) (soft
+        # labels, the cross-entropies' domain) for bce/ce
+        v1 = c_double()
+        fill(c, 102, False, 0.0, 1.0)
+        fill(b, 103, False, 0.0, 1.0)
+        for name, fn, extra, tg in (("mse_loss", lib.rtc_mse_loss, (), a),
+                                    ("l1_loss", lib.rtc_l1_loss, (), a),
+                                    ("smooth_l1_loss", lib.rtc_smooth_l1_loss, (1.0,), a),
+                                    ("binary_cross_entropy_loss", lib.rtc_binary_cross_entropy_loss,
+                                     (1e-7,), b),
+                                    ("cross_entropy_loss", lib.rtc_cross_entropy_loss, (1e-7,), b)):
+            timeit(name, f"cfg1 [{N1}]", 8 * N1,
+                   lambda fn=fn, extra=extra, tg=tg: N.check(fn(c[1].ref, tg[1].ref, *extra,
+                                                                byref(v1))))
+        del a, b, c
+    if "cfg2" in cfgs:   # cfg2
+        x = t([N2])
+        fill(x, 2, True, 0.0, 1.0)
+        sd = torch.zeros(1, dtype=torch.float64, device="cuda")
+        v = c_double()
+        timeit("sum (device result)", f"cfg2 [{N2}]", 4 * N2,
+               lambda: N.check(lib.rtc_sum_device(x[1].ref, c_void_p(sd.data_ptr()))))
+        for name, fn in (("sum", lib.rtc_sum), ("mean", lib.rtc_mean), ("max", lib.rtc_max),
+                         ("min", lib.rtc_min)):
+            timeit(name + " (host result)", f"cfg2 [{N2}]", 4 * N2,
+                   lambda fn=fn: N.check(fn(x[1].ref, byref(v))))
+        st4 = (c_double * 4)()
+        timeit("stats: sum+mean+max+min, one pass (host result)", f"cfg2 [{N2}]", 4 * N2,
+               lambda: N.check(lib.rtc_stats(x[1].ref, st4)))
+        del x
+    if "cfg3" in cfgs:   # cfg3
+        x = t([R3, C3])
+        fill(x, 3)
+        for dim, outn in ((1, R3), (0, C3)):
+            o = t([outn])
+            for name, fn in (("sum_dim", lib.rtc_sum_dim), ("mean_dim", lib.rtc_mean_dim),
+                             ("max_dim", lib.rtc_max_dim)):
+                timeit(f"{name}({dim})", f"cfg3 [{R3},{C3}]", 4 * R3 * C3 + 4 * outn,
+                       lambda fn=fn, o=o, dim=dim: N.check(fn(x[1].ref, dim, o[1].ref)))
+        del x
+    if "cfg4" in cfgs:   # cfg4
+        x, y = t([R4, C4]), t([R4, C4])
+        fill(x, 4, True, 0.0, 2.0)
+        for name in ("relu", "gelu", "swish", "sigmoid", "tanh", "selu", "softsign", "mish",
+                     "softplus"):
+            fn = getattr(lib, "rtc_" + name)
+            timeit(name, f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+                   lambda fn=fn: N.check(fn(x[1].ref, y[1].ref)))
+        timeit("leaky_relu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+               lambda: N.check(lib.rtc_leaky_relu(x[1].ref, y[1].ref, 0.01)))
+        timeit("elu", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+               lambda: N.check(lib.rtc_elu(x[1].ref, y[1].ref, 1.0)))
+        timeit("softmax(1)", f"cfg4 [{R4},{C4}]", 8 * R4 * C4,
+               lambda: N.check(lib.rtc_softmax(x[1].ref, 1, y[1].ref)))
+        bias = t([C4])
+        fill(bias, 9)
+        timeit("add_broadcast (row bias)", f"cfg4 [{R4},{C4}] + [{C4}]", 8 * R4 * C4 + 4 * C4,
+               lambda: N.check(lib.rtc_add_broadcast(x[1].ref, bias[1].ref, y[1].ref)))
+        # autograd backward (autograd/ops.rs) on cfg4's shape
+        g, z, w = t([R4, C4]), t([R4, C4]), t([R4, C4])
+        fill(g, 10, True, 0.0, 1.0)
+        fill(z, 11, True, 1.0, 0.5)
+        for name in ("relu", "sigmoid", "tanh", "gelu"):
+            fn = getattr(lib, f"rtc_{name}_backward")
+            timeit(f"{name}_backward", f"cfg4 [{R4},{C4}]", 12 * R4 * C4,
+                   lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, y[1].ref)))
+        for name in ("mul", "div"):
+            fn = getattr(lib, f"rtc_{name}_backward")
+            timeit(f"{name}_backward (both grads)", f"cfg4 [{R4},{C4}]", 20 * R4 * C4,
+                   lambda fn=fn: N.check(fn(g[1].ref, x[1].ref, z[1].ref, y[1].ref, w[1].ref)))
+        cols, rows = t([1, C4]), t([R4, 1])
+        timeit("broadcast_add_backward -> [1,C]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * C4,
+               lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, cols[1].ref, None)))
+        timeit("broadcast_add_backward -> [R,1]", f"cfg4 [{R4},{C4}]", 4 * R4 * C4 + 4 * R4,
+               lambda: N.check(lib.rtc_broadcast_add_backward(g[1].ref, rows[1].ref, None)))
+        del x, y, g, z, w
+    if "cfg5" in cfgs:   # cfg5
+        P = {k: t([N5]) for k in "pgmv"}
+        fill(P["p"], 51, True, 0.0, 0.02)
+        fill(P["g"], 52, True, 0.0, 1e-2)
+        fill(P["m"], 53, True, 0.0, 1e-3)
+        fill(P["v"], 54, False, 0.0, 1e-4)
+        timeit("adamw (in place)", f"cfg5 4x[{N5}]", 28 * N5,
+               lambda: N.check(lib.rtc_adamw_update(P["p"][1].ref, P["g"][1].ref, P["m"][1].ref,
+                                                    P["v"][1].ref, lr, b1, b2, eps, wd, tt,
+                                                    P["p"][1].ref, P["m"][1].ref, P["v"][1].ref)))
+
+def run_probe(args) -> None:
+    """Bandwidth probes (rtc_probe_stream): 1 GiB read with 16-byte loads
+    and through a cp.async.bulk ring, a 1 GiB copy, and sizings of cfg1's
+    fused add->mul_scalar map.  L2 flushed before each run, median of
+    max(5, --steps) runs; one JSON line per configuration."""
+    import torch
+
+    from rusttorch_b200 import _native as N
+
+    torch.cuda.set_device(0)
+    lib = N.lib()
+    stream = torch.cuda.current_stream()
+    N.check(lib.rtc_set_stream(c_void_p(stream.cuda_stream)))
+    peak, _ = peak_hbm()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    nbytes = 1 << 30
+    src = torch.randn(nbytes // 4, dtype=torch.float32, device="cuda")
+    dst = torch.empty_like(src)
+    only = re.compile(args.only) if args.only else None
+
+    def timeit(name, mode, nb, algo_bytes, p0, p1, p2, dirty=False):
+        """dirty=False: L2 flushed by writing 256 MiB and then reading another
+        256 MiB, so the timed kernel starts on clean lines; dirty=True: the
+        write alone, so the kernel also writes back up to an L2 of dirty lines."""
+        if only is not None and not only.search(name):
+            return
+        call = lambda: N.check(lib.rtc_probe_stream(mode, c_void_p(src.data_ptr()),
+                                                    c_void_p(dst.data_ptr()), nb, p0, p1, p2))
+        for _ in range(2):
+            call()
+        times = []
+        for _ in range(max(5, args.steps)):
+            flush.zero_()
+            if not dirty:
+                flush_rd.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        N.check(lib.rtc_synchronize())
+        ms = statistics.median(times)
+        gbs = algo_bytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"probe": name, "mode": mode, "p": [p0, p1, p2], "ms": ms, "GB_s": gbs,
+                          "frac_of_measured_peak": gbs / peak, "bytes": algo_bytes,
+                          "l2": "dirty" if dirty else "clean"}), flush=True)
+
+    # u < 0: the stats kernel with float32 trees per float4 (|u| loads in flight)
+    for threads, u, bps in ((256, 8, 0), (512, 4, 0), (512, 8, 0), (256, -4, 0), (256, -8, 0),
+                            (512, -4, 0), (512, -8, 0), (1024, -4, 0), (512, -8, 2),
+                            (256, -8, 4), (256, -8, 6), (-512, -8, 0), (-512, 8, 0)):
+        timeit(f"stats kernel t{threads} u{u} b{bps}", 7, nbytes, nbytes, threads, u, bps)
+    for dirty in (False, True):
+        tag = "dirty-L2" if dirty else "clean-L2"
+        timeit(f"{tag} cfg1 add->mul_scalar product", 5, 8 * N1, 12 * N1, 0, 4, 32, dirty)
+        timeit(f"{tag} read ldg t512 u4 b4", 0, nbytes, nbytes, 512, 4, 4, dirty)
+        timeit(f"{tag} copy ldg/stg t256 u8 b8", 4, nbytes, 2 * nbytes, 256, 8, 8, dirty)
+    for threads in (256, 512, 1024):
+        for u in (4, 8, 16):
+            for bps in (1, 2, 4, 8):
+                if threads * bps > 2048:
+                    continue
+                timeit(f"read ldg grid-stride t{threads} u{u} b{bps}", 0, nbytes, nbytes,
+                       threads, u, bps)
+                timeit(f"read ldg contiguous t{threads} u{u} b{bps}", 1, nbytes, nbytes,
+                       threads, u, bps)
+    for chunk in (4096, 8192, 16384, 32768):
+        for slots in (2, 4, 6, 8, 12, 16):
+            for ctas in (1, 2, 4):
+                if chunk * slots * ctas > 200 * 1024 or chunk * slots > 200 * 1024:
+                    continue
+                if chunk * slots * ctas < 32 * 1024:
+                    continue
+                timeit(f"read bulk ring c{chunk} s{slots} x{ctas}", 2, nbytes, nbytes,
+                       chunk, slots, ctas)
+                timeit(f"read bulk ring+fold c{chunk} s{slots} x{ctas}", 3, nbytes, nbytes,
+                       chunk, slots, ctas)
+    for u in (4, 8):
+        for bps in (4, 8):
+            timeit(f"copy ldg/stg t256 u{u} b{bps}", 4, nbytes, 2 * nbytes, 256, u, bps)
+    n1 = N1
+    for mode, label in ((5, "grid-stride"), (6, "balanced")):
+        for u in (1, 2, 4, 8):
+            for bps in ((-1, 0, 2, 4, 8, 16, 32, 64) if mode == 5 else (0, 1, 2, 4, 8, 16)):
+                timeit(f"cfg1 add->mul_scalar {label} u{u} b{bps}", mode, 8 * n1, 12 * n1,
+                       0, u, bps)
 
 
 if __name__ == "__main__":
-    main()
+    if "--probe" in sys.argv:
+        ap = argparse.ArgumentParser()
+        ap.add_argument("--probe", action="store_true")
+        ap.add_argument("--steps", type=int, default=9)
+        ap.add_argument("--only", default="")
+        run_probe(ap.parse_args())
+    else:
+        main()

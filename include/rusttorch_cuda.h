@@ -120,6 +120,26 @@ rtc_result rtc_selftest_bounded_wait(void);
  * order of Iterator::sum with init = -0.0), bit for bit. */
 rtc_result rtc_selftest_ordered_sum(const rtc_tensor* x, int chains, float init,
                                     float* out_value);
+/* Math mode of the transcendental activations (sigmoid, tanh, gelu, swish,
+ * mish, softplus) and softmax; no reference counterpart.
+ *  RTC_MATH_TOLERANCE (default): within 1e-6 relative error or 4 ulp of the
+ *    reference's result on every float input, from single-precision
+ *    exp/tanh/log (at most 5.8e-7 relative over all 2^32 inputs); where the
+ *    reference's own formula cancels (gelu's 1 + tanh for inputs below
+ *    -1.58, softplus and mish's 1 + exp) the exact glibc steps are kept.
+ *  RTC_MATH_EXACT: glibc's expf/tanhf reproduced bit for bit (softplus and
+ *    mish still use a correctly rounded log: within 1 and 6 ulp).
+ * Process-wide; the environment variable RTC_MATH_MODE=exact|tolerance sets
+ * the initial mode.  Kernels already queued keep the mode they were queued
+ * with.  ELU, SELU, the backward ops and the losses are the same in both. */
+enum { RTC_MATH_TOLERANCE = 0, RTC_MATH_EXACT = 1 };
+rtc_result rtc_set_math_mode(int mode);
+int rtc_get_math_mode(void);
+/* Test hook (no reference counterpart): out[i] = the tolerance mode's
+ * primitive `which` of x[i] on the current GPU (0 exp, 1 log for positive
+ * normal x, 2 tanh, 3 the correctly rounded reciprocal for x in [1, 2^64]);
+ * device pointers, returns once queued. */
+rtc_result rtc_selftest_fastmath(int which, const float* x, float* out, size_t n);
 int rtc_device_count(void);
 /* The calling thread's current GPU (host-memory ops and the flat *_f32 API
  * run there). */
@@ -399,6 +419,24 @@ rtc_result rtc_mean_backward(const rtc_tensor* grad_output, const rtc_tensor* gr
  * for equal element counts, else result[i % m] += grad[i].  Device only. */
 rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
                                       const rtc_tensor* grad_b);
+
+/* ------------------------------------------------------------ diagnostics */
+/* Bandwidth probes (no reference counterpart): the read ceiling the
+ * reductions are judged against and the sizing of the small fused map.
+ * mode 0/1: read `bytes` of src with 16-byte loads, p1 (4, 8, 16) loads in
+ * flight per thread, p0 threads per block, p2 blocks per SM (0: grid-stride,
+ * 1: one contiguous range per block); 2/3: read src through a cp.async.bulk
+ * ring into shared memory, p1 slots of p0 bytes per CTA, p2 CTAs per SM (3:
+ * every thread also folds each slot); 4: copy src to dst as mode 0; 5/6: the
+ * add->mul_scalar map over a = src, b = src + bytes/2 into dst with U = p1
+ * (1, 2, 4, 8) and p2 blocks per SM (5: grid-stride, p2 = 0 one resident
+ * wave, p2 < 0 one block per tile; 6: one balanced range per block); 7: the
+ * global sum/max/min kernel over bytes/4 floats of src with p0 threads, |p1|
+ * loads in flight per thread (p1 < 0: each float4 summed as a float32 tree)
+ * and p2 blocks per SM (0: all that stay resident).
+ * Device pointers on the current GPU, 16-byte aligned; returns once queued. */
+rtc_result rtc_probe_stream(int mode, const void* src, void* dst, size_t bytes, int p0, int p1,
+                            int p2);
 
 /* ------------------------------------- flat float32 API (device pointers) */
 /* rusttorch_relu_f32 / add_f32 / mul_f32, ffi/ops.rs:348-389: contiguous f32

@@ -28,12 +28,43 @@ __all__ = [
     "adam_update", "adamw_update", "sgd_update", "sgd_momentum_update",
     "add_broadcast", "sub_broadcast", "mul_broadcast", "div_broadcast",
     "nn_adam_step", "nn_sgd_step",
-    "synchronize",
+    "synchronize", "set_math_mode", "get_math_mode", "math_mode",
 ]
 
 
 def version() -> str:
     return lib().rtc_version().decode()
+
+
+def set_math_mode(mode: str) -> None:
+    """"tolerance" (the default: within 1e-6 relative error or 4 ulp of the
+    reference's glibc results, single-precision exp/tanh/log) or "exact"
+    (glibc's expf/tanhf bit for bit) for the transcendental activations and
+    softmax.  Process-wide (rtc_set_math_mode)."""
+    code = {"tolerance": _native.MATH_TOLERANCE, "exact": _native.MATH_EXACT}.get(mode)
+    if code is None:
+        raise ValueError(f"math mode must be 'tolerance' or 'exact', not {mode!r}")
+    check(lib().rtc_set_math_mode(code))
+
+
+def get_math_mode() -> str:
+    return "exact" if lib().rtc_get_math_mode() == _native.MATH_EXACT else "tolerance"
+
+
+class math_mode:
+    """Context manager: `with math_mode("exact"): ...` restores the previous
+    mode on exit."""
+
+    def __init__(self, mode: str):
+        self.mode = mode
+
+    def __enter__(self):
+        self.before = get_math_mode()
+        set_math_mode(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        set_math_mode(self.before)
 
 
 def synchronize() -> None:

@@ -15,6 +15,8 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "librusttorch_cuda.so"
 HEADER_PATH = PKG.parent / "include" / "rusttorch_cuda.h"
 
+# math modes (rtc_set_math_mode)
+MATH_TOLERANCE, MATH_EXACT = 0, 1
 # dtype codes and status codes (rusttorch_cuda.h)
 F32, F64, I32, I64 = 0, 1, 2, 3
 OK, SHAPE_MISMATCH, DTYPE_MISMATCH, EMPTY_TENSOR, INVALID_DIMENSION, INVALID_ARGUMENT, \
@@ -152,6 +154,10 @@ _SIGNATURES = {
     "rtc_relu_f32": (RtcResult, [c_void_p, c_void_p, c_size_t]),
     "rtc_add_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),
     "rtc_mul_f32": (RtcResult, [c_void_p, c_void_p, c_void_p, c_size_t]),
+    "rtc_probe_stream": (RtcResult, [c_int, c_void_p, c_void_p, c_size_t, c_int, c_int, c_int]),
+    "rtc_set_math_mode": (RtcResult, [c_int]),
+    "rtc_get_math_mode": (c_int, []),
+    "rtc_selftest_fastmath": (RtcResult, [c_int, c_void_p, c_void_p, c_size_t]),
 }
 
 _lib = None

@@ -71,6 +71,15 @@ extern "C" rtc_result rtc_selftest_bounded_wait(void) {
   return launched(launch_bounded_wait_probe(device, thread_stream()), "selftest_bounded_wait");
 }
 
+extern "C" rtc_result rtc_set_math_mode(int mode) {
+  if (mode != RTC_MATH_TOLERANCE && mode != RTC_MATH_EXACT)
+    return invalid_argument("mode", "must be RTC_MATH_TOLERANCE or RTC_MATH_EXACT");
+  set_math_exact(mode == RTC_MATH_EXACT);
+  return ok();
+}
+
+extern "C" int rtc_get_math_mode(void) { return math_exact() ? RTC_MATH_EXACT : RTC_MATH_TOLERANCE; }
+
 extern "C" int rtc_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;

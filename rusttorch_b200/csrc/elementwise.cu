@@ -15,6 +15,9 @@
 #include "rt_ops.cuh"
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -42,24 +45,53 @@ float gelu_k() {
   return sqrtf(two / pi);
 }
 
+namespace {
+// -1: not yet read from RTC_MATH_MODE; 0: tolerance; 1: exact.
+std::atomic<int> g_math_mode{-1};
+}  // namespace
+
+bool math_exact() {
+  int m = g_math_mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    const char* env = std::getenv("RTC_MATH_MODE");
+    const int want = (env && std::strcmp(env, "exact") == 0) ? 1 : 0;
+    int expected = -1;
+    g_math_mode.compare_exchange_strong(expected, want);
+    m = g_math_mode.load(std::memory_order_relaxed);
+  }
+  return m == 1;
+}
+
+void set_math_exact(bool exact) { g_math_mode.store(exact ? 1 : 0); }
+
 cudaError_t launch_unary(UnaryOp op, float param, const float* x, float* out, size_t n,
                          cudaStream_t s) {
   In<1> in{{x}};
+  const bool exact = math_exact();
   switch (op) {
     case kRelu: return launch_map(OpRelu{}, in, out, n, s);
     case kLeakyRelu: return launch_map(OpLeakyRelu{param}, in, out, n, s);
-    case kSigmoid: return launch_map(OpSigmoid{}, in, out, n, s);
-    case kTanh: return launch_map(OpTanh{}, in, out, n, s);
-    case kGelu: return launch_map(OpGelu{gelu_k()}, in, out, n, s);
-    case kSwish: return launch_map(OpSwish{}, in, out, n, s);
+    case kSigmoid:
+      return exact ? launch_map(OpSigmoid{}, in, out, n, s)
+                   : launch_map(OpSigmoidTol{}, in, out, n, s);
+    case kTanh:
+      return exact ? launch_map(OpTanh{}, in, out, n, s) : launch_map(OpTanhTol{}, in, out, n, s);
+    case kGelu:
+      return exact ? launch_map(OpGelu{gelu_k()}, in, out, n, s)
+                   : launch_map_split(OpGeluTol{gelu_k()}, x, out, n, s);
+    case kSwish:
+      return exact ? launch_map(OpSwish{}, in, out, n, s) : launch_map(OpSwishTol{}, in, out, n, s);
     case kElu: return launch_map(OpElu{param}, in, out, n, s);
     case kSelu: {
       // activation.rs:236-251: f64 constants, cast to f32 at use.
       const float alpha = (float)1.6732632423543772, scale = (float)1.0507009873554805;
       return launch_map(OpSelu{alpha, scale}, in, out, n, s);
     }
-    case kMish: return launch_map(OpMish{}, in, out, n, s);
-    case kSoftplus: return launch_map(OpSoftplus{}, in, out, n, s);
+    case kMish:
+      return exact ? launch_map(OpMish{}, in, out, n, s) : launch_map(OpMishTol{}, in, out, n, s);
+    case kSoftplus:
+      return exact ? launch_map(OpSoftplus{}, in, out, n, s)
+                   : launch_map(OpSoftplusTol{}, in, out, n, s);
     case kSoftsign: return launch_map(OpSoftsign{}, in, out, n, s);
     case kAddScalar: return launch_map(OpAddScalar{param}, in, out, n, s);
     case kMulScalar: return launch_map(OpMulScalar{param}, in, out, n, s);

@@ -106,14 +106,50 @@ __device__ void block_reduce(Acc& a) {
   }
 }
 
+// max/min of three floats in one instruction (sm_100a); NaN inputs are
+// ignored as fmaxf/fminf ignore them, and the host repairs the NaN and zero
+// cases exactly as for fmaxf/fminf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// f64 value of x + y + z + w.  F32TREE: (x + y) + (z + w) in float32 and
+// converted once — two roundings on each element's path, so the error is at
+// most 2^-23 of |x| + |y| + |z| + |w| (the sum's tolerance is 1e-6 of
+// sum|x|) — unless that overflows, when the tree is redone in float64 (an
+// infinite or NaN input gives the same infinity or NaN either way).
+// Otherwise every float is converted exactly and added in float64.
+template <bool F32TREE>
+__device__ __forceinline__ double sum4(const float4& v) {
+  if (F32TREE) {
+    const float t = fadd(fadd(v.x, v.y), fadd(v.z, v.w));
+    if (fabsf(t) != INFINITY) return (double)t;
+  }
+  return dadd(dadd((double)v.x, (double)v.y), dadd((double)v.z, (double)v.w));
+}
+
 // Block b reduces the contiguous element range [b*chunk, (b+1)*chunk) with
-// 16-byte loads (the unaligned head and the tail are read as scalars).
-__global__ void __launch_bounds__(kStatsThreads)
+// 16-byte loads (the unaligned head and the tail are read as scalars).  U
+// loads per thread are in flight at once; each float4 is reduced as a tree
+// (sum4, and three-input max/min) into one of two accumulators, so the
+// dependent operations between one batch of loads and the next stay few: a
+// warp spends most of its time with loads in flight, which is what a
+// read-only stream needs to reach HBM bandwidth.
+template <int NT, int U, bool F32TREE>
+__global__ void __launch_bounds__(NT)
 stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
   const size_t lo = (size_t)blockIdx.x * chunk;
   const size_t hi = min(n, lo + chunk);
   Acc a;
   a.init();
+  double s1 = 0.0;
   if (lo < hi) {
     const float* p = x + lo;
     const size_t cnt = hi - lo;
@@ -122,21 +158,21 @@ stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
     if (threadIdx.x < head) a.add(__ldcs(p + threadIdx.x));
     const float4* q = reinterpret_cast<const float4*>(p + head);
     const size_t n4 = (cnt - head) >> 2;
-    constexpr int U = 8;
     size_t i = threadIdx.x;
-    for (; i + (U - 1) * kStatsThreads < n4; i += U * kStatsThreads) {
+    for (; i + (U - 1) * NT < n4; i += U * NT) {
       float4 v[U];
 #pragma unroll
-      for (int u = 0; u < U; u++) v[u] = __ldcs(q + i + u * kStatsThreads);
+      for (int u = 0; u < U; u++) v[u] = __ldcs(q + i + u * NT);
 #pragma unroll
       for (int u = 0; u < U; u++) {
-        a.add(v[u].x);
-        a.add(v[u].y);
-        a.add(v[u].z);
-        a.add(v[u].w);
+        const double t = sum4<F32TREE>(v[u]);
+        if (u & 1) s1 = dadd(s1, t);
+        else a.s = dadd(a.s, t);
+        a.mx = fmax3(fmax3(a.mx, v[u].x, v[u].y), v[u].z, v[u].w);
+        a.mn = fmin3(fmin3(a.mn, v[u].x, v[u].y), v[u].z, v[u].w);
       }
     }
-    for (; i < n4; i += kStatsThreads) {
+    for (; i < n4; i += NT) {
       const float4 v = __ldcs(q + i);
       a.add(v.x);
       a.add(v.y);
@@ -146,7 +182,8 @@ stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
     const size_t done = head + (n4 << 2);
     if (threadIdx.x < cnt - done) a.add(__ldcs(p + done + threadIdx.x));
   }
-  block_reduce<kStatsThreads>(a);
+  a.s = dadd(a.s, s1);
+  block_reduce<NT>(a);
   if (threadIdx.x == 0) parts[blockIdx.x] = StatsPart{a.s, a.mx, a.mn};
 }
 
@@ -690,24 +727,87 @@ cudaError_t strip_launch(const float* x, size_t outer, size_t len, size_t inner,
   return cudaGetLastError();
 }
 
+// The stats kernel's shape: threads per block, loads in flight per thread,
+// and the blocks per SM that stay resident together (so that one wave of
+// blocks covers the tensor and every block streams the same number of bytes).
+struct StatsShape {
+  int threads, u;
+  bool f32tree;
+};
+constexpr StatsShape kStatsShape{512, 8, true};
+
+template <int NT, int U, bool T>
+int stats_resident(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, stats_kernel<NT, U, T>, NT, 0) !=
+          cudaSuccess || n < 1)
+    n = 1;
+  if (device >= 0 && device < 64) cached[device] = n;
+  return n;
+}
+
+template <int NT, int U, bool T>
+cudaError_t launch_stats_shape(const float* x, size_t n, StatsPart* parts, int nparts,
+                               StatsPart* out, cudaStream_t s, double* sum_out,
+                               bool combine = true) {
+  const size_t chunk = (n + (size_t)nparts - 1) / (size_t)nparts;
+  stats_kernel<NT, U, T><<<nparts, NT, 0, s>>>(x, n, chunk ? chunk : 1, parts);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !combine) return e;
+  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out, sum_out);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
-int stats_max_parts(int device) { return sm_count(device) * 4; }
+int stats_max_parts(int device) {
+  return sm_count(device) *
+         stats_resident<kStatsShape.threads, kStatsShape.u, kStatsShape.f32tree>(device);
+}
 
 int stats_num_parts(int device, size_t n) {
-  // At least ~16K elements per block so that small inputs use few blocks.
+  // At least ~16K elements per block so that small inputs use few blocks;
+  // at most one resident wave.
   const size_t want = (n + 16383) / 16384;
   return (int)std::max<size_t>(1, std::min<size_t>(want, (size_t)stats_max_parts(device)));
 }
 
 cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
                          cudaStream_t s, double* sum_out) {
-  const size_t chunk = (n + (size_t)nparts - 1) / (size_t)nparts;
-  stats_kernel<<<nparts, kStatsThreads, 0, s>>>(x, n, chunk ? chunk : 1, parts);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out, sum_out);
-  return cudaGetLastError();
+  return launch_stats_shape<kStatsShape.threads, kStatsShape.u, kStatsShape.f32tree>(
+      x, n, parts, nparts, out, s, sum_out);
+}
+
+cudaError_t launch_stats_variant(int threads, int u, int blocks_per_sm, const float* x, size_t n,
+                                 StatsPart* parts, int max_parts, cudaStream_t s,
+                                 double* sum_out) {
+  const int dev = cur_device();
+  const size_t want = (n + 16383) / 16384;
+  // u < 0: float32 trees per float4 (sum4<true>) with |u| loads in flight;
+  // threads < 0: the partials only, without the combining kernel
+  const bool combine = threads > 0;
+  if (threads < 0) threads = -threads;
+  const bool tree = u < 0;
+  const int uu = tree ? -u : u;
+#define RT_STATS_VARIANT(NT, UU, T)                                                       \
+  if (threads == NT && uu == UU && tree == T) {                                           \
+    const int per = blocks_per_sm > 0 ? blocks_per_sm : stats_resident<NT, UU, T>(dev);   \
+    const int np = (int)std::max<size_t>(                                                 \
+        1, std::min<size_t>(want, std::min<size_t>((size_t)per * sm_count(dev), max_parts))); \
+    return launch_stats_shape<NT, UU, T>(x, n, parts, np, nullptr, s, sum_out, combine);  \
+  }
+  RT_STATS_VARIANT(256, 8, false)
+  RT_STATS_VARIANT(512, 4, false)
+  RT_STATS_VARIANT(512, 8, false)
+  RT_STATS_VARIANT(256, 4, true)
+  RT_STATS_VARIANT(256, 8, true)
+  RT_STATS_VARIANT(512, 4, true)
+  RT_STATS_VARIANT(512, 8, true)
+  RT_STATS_VARIANT(1024, 4, true)
+#undef RT_STATS_VARIANT
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStream_t s) {

@@ -14,6 +14,14 @@ constexpr int kThreads = 256;
 // Number of SMs of `device` (cached after the first query).
 int sm_count(int device);
 
+// ------------------------------------------------------------------ math mode
+// Whether the transcendental activations and softmax reproduce glibc's bits
+// (exact) or stay within 1e-6 relative error / 4 ulp of them (tolerance, the
+// default).  Process-wide; the RTC_MATH_MODE environment variable ("exact" or
+// "tolerance") sets the initial value.
+bool math_exact();
+void set_math_exact(bool exact);
+
 // ---------------------------------------------------------------- elementwise
 enum UnaryOp {
   kRelu, kLeakyRelu, kSigmoid, kTanh, kGelu, kSwish, kElu, kSelu, kMish, kSoftplus, kSoftsign,
@@ -89,6 +97,13 @@ int stats_max_parts(int device);
 // `parts` is scratch of stats_num_parts(device, n) entries.
 cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
                          cudaStream_t s, double* sum_out = nullptr);
+
+// launch_stats with another kernel shape (threads 256/512/1024, U loads in
+// flight per thread, blocks_per_sm <= 0: as many as stay resident) and at
+// most max_parts partials; the sum alone goes to *sum_out.  For the probes.
+cudaError_t launch_stats_variant(int threads, int u, int blocks_per_sm, const float* x, size_t n,
+                                 StatsPart* parts, int max_parts, cudaStream_t s,
+                                 double* sum_out);
 
 // Positions used by the exact repair path, 1-based (0 = none).
 struct IndexScan {

@@ -141,6 +141,93 @@ cudaError_t launch_map(const F& f, const In<NIN>& in, float* out, size_t n, cuda
 }
 
 
+// Map for a rule with a cheap path and an expensive one that only some
+// elements need (GELU in the tolerance math mode): F provides arg(x),
+// needs_exact(z), fast_tanh(z), exact_tanh(z) and finish(x, t).  Every
+// thread runs the cheap path on its elements; the arguments of the elements
+// that need the expensive path are queued in the warp's shared memory (slot
+// = the warp's running count plus the lanes below in a ballot), the whole
+// warp then evaluates the queue 32 arguments at a time, and each element
+// picks up its result from its slot.  So the expensive path runs on full
+// warps, once per queued element, instead of on every warp that holds one
+// such element (which, for inputs spread as the BASELINE configs are, is
+// every warp).  Results equal F's per-element operator() bit for bit.
+constexpr int kSplitU = 2;
+
+template <class F>
+__global__ void __launch_bounds__(kThreads)
+map_split_kernel(const float* x, float* out, size_t n, F f) {
+  __shared__ float queue[kThreads / 32][32 * 4 * kSplitU];
+  const unsigned lane = threadIdx.x & 31u;
+  float* wq = queue[threadIdx.x >> 5];
+  const unsigned below = (1u << lane) - 1u;
+  const size_t n4 = n >> 2;
+  const size_t tile = (size_t)kThreads * kSplitU;
+  // Every lane of a warp runs the same number of iterations (the loop bound
+  // is rounded up to whole warps), so the ballots see all 32 lanes.
+  const size_t warp0 = (size_t)blockIdx.x * tile + (threadIdx.x & ~31u);
+  for (size_t wbase = warp0; wbase < n4; wbase += (size_t)gridDim.x * tile) {
+    const size_t base = wbase + lane;
+    float xs[4 * kSplitU], t[4 * kSplitU];
+    int slot[4 * kSplitU];
+#pragma unroll
+    for (int u = 0; u < kSplitU; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      const float4 v = j < n4 ? ld4(x + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xs[4 * u] = v.x;
+      xs[4 * u + 1] = v.y;
+      xs[4 * u + 2] = v.z;
+      xs[4 * u + 3] = v.w;
+    }
+    int count = 0;
+#pragma unroll
+    for (int e = 0; e < 4 * kSplitU; e++) {
+      const float z = f.arg(xs[e]);
+      const bool valid = base + (size_t)(e / 4) * kThreads < n4;
+      const bool need = valid && F::needs_exact(z);
+      t[e] = F::fast_tanh(z);
+      const unsigned m = __ballot_sync(0xffffffffu, need);
+      slot[e] = need ? count + __popc(m & below) : -1;
+      if (need) wq[slot[e]] = z;
+      count += __popc(m);
+    }
+    __syncwarp();
+    for (int k = (int)lane; k < count; k += 32) wq[k] = F::exact_tanh(wq[k]);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 4 * kSplitU; e++)
+      if (slot[e] >= 0) t[e] = wq[slot[e]];
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kSplitU; u++) {
+      const size_t j = base + (size_t)u * kThreads;
+      if (j < n4)
+        st4(out + 4 * j, make_float4(F::finish(xs[4 * u], t[4 * u]),
+                                     F::finish(xs[4 * u + 1], t[4 * u + 1]),
+                                     F::finish(xs[4 * u + 2], t[4 * u + 2]),
+                                     F::finish(xs[4 * u + 3], t[4 * u + 3])));
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const size_t i = (n4 << 2) + threadIdx.x;
+    out[i] = f(x[i]);
+  }
+}
+
+template <class F>
+cudaError_t launch_map_split(const F& f, const float* x, float* out, size_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if (aligned16(x) && aligned16(out)) {
+    const unsigned grid =
+        grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * kSplitU, 32);
+    map_split_kernel<F><<<grid, kThreads, 0, s>>>(x, out, n, f);
+  } else {
+    In<1> in{{x}};
+    map_scalar_kernel<F, 1><<<grid_for(n, kThreads), kThreads, 0, s>>>(in, out, n, f);
+  }
+  return cudaGetLastError();
+}
+
 // Two outputs from one pass: f returns a float2 {out0, out1}.
 template <class F, int NIN>
 __device__ __forceinline__ float2 apply2(const F& f, const In<NIN>& in, size_t i) {

@@ -4,6 +4,7 @@
 // device).  Citations are to rusttorch-core/src/ops/.
 #pragma once
 
+#include "rt_fastmath.cuh"
 #include "rt_libm.cuh"
 
 namespace rt {
@@ -105,6 +106,93 @@ struct OpMish {
 // :351 softsign = x / (1 + |x|)
 struct OpSoftsign {
   RT_HD float operator()(float x) const { return fdiv(x, fadd(1.0f, fabsf(x))); }
+};
+
+// ---- the same activations in the tolerance math mode ---------------------
+// Within north_star's 1e-6 relative error or 4 ulp of the reference's formula
+// over glibc, on every float input (tests/native/fastmath_check.cpp), from
+// the single-precision functions of rt_fastmath.cuh.
+//
+// glibc's expf(t) is +inf exactly for t >= 88.72283935546875 (0x42b17218),
+// so the reference's 1/(1 + exp(-x)) is +0 and x/(1 + exp(-x)) is -0 for
+// x <= -88.72283935546875; below that the result would otherwise be a tiny
+// nonzero value.
+constexpr float kExpOverflowNeg = -88.72283935546875f;
+
+// :21 sigmoid.  With e = exp(-|x|): 1/(1 + e) for x >= 0 and e/(1 + e) for
+// x < 0 (the same value; the second form never overflows, and its result,
+// scaled last, is rounded once when it is subnormal).
+struct OpSigmoidTol {
+  RT_HD float operator()(float x) const {
+    const float na = u2f(f2u(x) | 0x80000000u);          // -|x|
+    const ExpParts e = exp_parts(na < -104.0f ? -104.0f : na);
+    const float r = rcp_cr(fadd(1.0f, fmul(fmul(e.p, e.s1), e.s2)));
+    const float y = x < 0.0f ? fmul(fmul(fmul(e.p, r), e.s1), e.s2) : r;
+    return x <= kExpOverflowNeg ? 0.0f : y;
+  }
+};
+// :263 swish = x/(1 + exp(-x)), the same way (x*e/(1 + e) for x < 0).
+struct OpSwishTol {
+  RT_HD float operator()(float x) const {
+    const float na = u2f(f2u(x) | 0x80000000u);
+    const ExpParts e = exp_parts(na < -104.0f ? -104.0f : na);
+    const float r = rcp_cr(fadd(1.0f, fmul(fmul(e.p, e.s1), e.s2)));
+    const float y = x < 0.0f ? fmul(fmul(fmul(fmul(e.p, r), x), e.s1), e.s2) : fmul(x, r);
+    return x <= kExpOverflowNeg ? fmul(x, 0.0f) : y;
+  }
+};
+// :40 tanh
+struct OpTanhTol {
+  RT_HD float operator()(float x) const { return tanh_fast(x); }
+};
+// :319 softplus = x > 20 ? x : ln(1 + exp(x)).  1 + exp(x) is the
+// reference's float bit for bit (expf_glibc): for x well below 0 its last bit
+// decides the result's leading digits, and only the log is approximated.
+struct OpSoftplusTol {
+  RT_HD float operator()(float x) const {
+    return x > 20.0f ? x : log_fast(fadd(1.0f, expf_glibc(x)));
+  }
+};
+// :284 mish = x * tanh(softplus(x)).  With y = 1 + exp(x) (the reference's
+// float, as in softplus), tanh(ln y) = (y^2 - 1)/(y^2 + 1) =
+// (y - 1)(y + 1)/(y*y + 1): no log and no tanh, and y - 1 is exact.  For
+// x > 20 the reference's tanh(x) is 1, so mish is x.
+struct OpMishTol {
+  RT_HD float operator()(float x) const {
+    const float y = fadd(1.0f, expf_glibc(x));
+    const float num = fmul(fsub(y, 1.0f), fadd(y, 1.0f));
+    const float t = fmul(num, rcp_cr(ffma(y, y, 1.0f)));
+    return x > 20.0f ? x : fmul(x, t);
+  }
+};
+
+// :61 gelu.  1 + tanh(z) cancels for z well below 0: there the reference's
+// result is the gap between -1 and glibc's tanhf(z), and it carries no more
+// than a few of tanhf's bits, so tanhf must be glibc's to the last bit
+// (tanhf_glibc).  Above kGeluExactBelow (1 + tanh(z) > 0.115) the
+// cancellation magnifies the fast tanh's error by less than 9 and the result
+// stays within 5.8e-7 of the reference's; below -9.1 glibc's tanhf is
+// exactly -1.  The kernel sends only the middle range through
+// tanhf_glibc (rt_map.cuh, map_split_kernel).
+#ifndef RT_GELU_EXACT_BELOW
+#define RT_GELU_EXACT_BELOW -1.4f
+#endif
+constexpr float kGeluExactBelow = RT_GELU_EXACT_BELOW;
+struct OpGeluTol {
+  float k;
+  // z = k*(x + 0.044715*x^3), in the reference's order
+  RT_HD float arg(float x) const {
+    const float x3 = fmul(fmul(x, x), x);
+    return fmul(k, fadd(x, fmul(0.044715f, x3)));
+  }
+  RT_HD static bool needs_exact(float z) { return z < kGeluExactBelow && z >= -9.1f; }
+  RT_HD static float fast_tanh(float z) { return z < -9.1f ? -1.0f : tanh_fast(z); }
+  RT_HD static float exact_tanh(float z) { return tanhf_glibc(z); }
+  RT_HD static float finish(float x, float t) { return fmul(fmul(0.5f, x), fadd(1.0f, t)); }
+  RT_HD float operator()(float x) const {
+    const float z = arg(x);
+    return finish(x, needs_exact(z) ? exact_tanh(z) : fast_tanh(z));
+  }
 };
 
 // ---- ordering rules of Iterator::max_by / min_by with partial_cmp ---------

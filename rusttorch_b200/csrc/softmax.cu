@@ -9,7 +9,10 @@
 // minimum-stride axis is still the last one).
 //
 // Every exponent is x - m <= 0 (or NaN), so the exponential is
-// expf_glibc_nonpos, which skips expf's overflow branches.
+// expf_glibc_nonpos (exact math mode), which skips expf's overflow branches,
+// or exp_fast_nonpos (tolerance mode, rt_fastmath.cuh): the kernels take it
+// as the template parameter EXP.  Only the exponential changes between the
+// modes; the sum keeps ndarray's order in both.
 //
 // Why m may be computed with fmaxf: the fold and fmaxf agree on every lane
 // without NaN except for the sign of a zero maximum, and x - (+0) and x - (-0)
@@ -31,6 +34,13 @@ namespace rt {
 namespace {
 
 constexpr int kRowThreads = 256;
+
+struct ExpExact {
+  __device__ __forceinline__ static float f(float x) { return expf_glibc_nonpos(x); }
+};
+struct ExpTol {
+  __device__ __forceinline__ static float f(float x) { return exp_fast_nonpos(x); }
+};
 
 // e / s for a lane-constant s, without a division per element: with
 // r = 1/s rounded to double, (float)(e * r) equals the IEEE f32 quotient
@@ -94,6 +104,7 @@ __device__ float chain_sum8(const float* e, size_t len) {
   return acc;
 }
 
+template <class EXP>
 __global__ void __launch_bounds__(kRowThreads)
 softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
   extern __shared__ __align__(16) float e[];
@@ -121,7 +132,7 @@ softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
     }
   }
   m = block_max(m, red);   // contains __syncthreads: e[] is complete
-  for (size_t i = threadIdx.x; i < len; i += kRowThreads) e[i] = expf_glibc_nonpos(fsub(e[i], m));
+  for (size_t i = threadIdx.x; i < len; i += kRowThreads) e[i] = EXP::f(fsub(e[i], m));
   __syncthreads();
   if (threadIdx.x < 8) {
     const float s = chain_sum8(e, len);
@@ -148,7 +159,7 @@ softmax_row_kernel(const float* x, size_t rows, size_t len, float* out) {
 // sequential chain phase hides behind the other rows' memory traffic.
 constexpr int kRegThreads = 128;
 
-template <int VPT>
+template <int VPT, class EXP>
 __global__ void __launch_bounds__(kRegThreads)
 softmax_row_reg_kernel(const float* x, size_t len, float* out) {
   extern __shared__ __align__(16) float e[];
@@ -174,10 +185,10 @@ softmax_row_reg_kernel(const float* x, size_t len, float* out) {
   for (int i = 0; i < VPT; i++) {
     const int j = threadIdx.x + i * kRegThreads;
     if (j < n4) {
-      v[i].x = expf_glibc_nonpos(fsub(v[i].x, m));
-      v[i].y = expf_glibc_nonpos(fsub(v[i].y, m));
-      v[i].z = expf_glibc_nonpos(fsub(v[i].z, m));
-      v[i].w = expf_glibc_nonpos(fsub(v[i].w, m));
+      v[i].x = EXP::f(fsub(v[i].x, m));
+      v[i].y = EXP::f(fsub(v[i].y, m));
+      v[i].z = EXP::f(fsub(v[i].z, m));
+      v[i].w = EXP::f(fsub(v[i].w, m));
       es[j] = v[i];
     }
   }
@@ -197,17 +208,17 @@ softmax_row_reg_kernel(const float* x, size_t len, float* out) {
   }
 }
 
-template <int VPT>
+template <int VPT, class EXP>
 cudaError_t launch_row_reg(const float* x, size_t rows, size_t len, float* out, cudaStream_t s) {
   const size_t smem = len * sizeof(float);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(softmax_row_reg_kernel<VPT>,
+    cudaError_t e = cudaFuncSetAttribute(softmax_row_reg_kernel<VPT, EXP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   for (size_t r0 = 0; r0 < rows; r0 += 0x7fffffffull) {
     const size_t nr = std::min<size_t>(rows - r0, 0x7fffffffull);
-    softmax_row_reg_kernel<VPT><<<(unsigned)nr, kRegThreads, smem, s>>>(x + r0 * len, len,
+    softmax_row_reg_kernel<VPT, EXP><<<(unsigned)nr, kRegThreads, smem, s>>>(x + r0 * len, len,
                                                                         out + r0 * len);
   }
   return cudaGetLastError();
@@ -225,13 +236,14 @@ row_max_kernel(const float* x, size_t len, float* m_out) {
 }
 
 // Long rows, pass 2: out = exp(x - m).
+template <class EXP>
 __global__ void __launch_bounds__(kRowThreads)
 row_exp_kernel(const float* x, size_t len, const float* m, float* out) {
   const size_t row = blockIdx.y;
   const float mr = m[row];
   for (size_t i = (size_t)blockIdx.x * kRowThreads + threadIdx.x; i < len;
        i += (size_t)gridDim.x * kRowThreads)
-    out[row * len + i] = expf_glibc_nonpos(fsub(x[row * len + i], mr));
+    out[row * len + i] = EXP::f(fsub(x[row * len + i], mr));
 }
 
 // Long rows, pass 3: s per row, eight sequential chains (one warp per row).
@@ -255,6 +267,7 @@ row_div_kernel(float* out, size_t len, const float* s) {
 
 // dim is not the last axis: one thread per (outer, inner) lane, three passes
 // along len; the sum is ndarray's row-order chain res = res + e_l.
+template <class EXP>
 __global__ void __launch_bounds__(kThreads)
 softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, float* out) {
   const size_t lanes = outer * inner;
@@ -267,7 +280,7 @@ softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, floa
     for (size_t l = 0; l < len; l++) m = fmaxf(m, p[l * inner]);
     float s = 0.0f;
     for (size_t l = 0; l < len; l++) {
-      const float ev = expf_glibc_nonpos(fsub(p[l * inner], m));
+      const float ev = EXP::f(fsub(p[l * inner], m));
       q[l * inner] = ev;
       s = fadd(s, ev);
     }
@@ -276,10 +289,9 @@ softmax_lane_kernel(const float* x, size_t outer, size_t len, size_t inner, floa
   }
 }
 
-}  // namespace
-
-cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner,
-                           bool last_axis, float* out, cudaStream_t s) {
+template <class EXP>
+cudaError_t launch_softmax_exp(const float* x, size_t outer, size_t len, size_t inner,
+                               bool last_axis, float* out, cudaStream_t s) {
   if (outer == 0 || len == 0 || inner == 0) return cudaSuccess;
   // A non-last axis followed only by length-1 axes has contiguous lanes but
   // ndarray's row-order chain for the sum: short lanes take the lane kernel,
@@ -291,27 +303,27 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
     const size_t lanes = outer * inner;
     const unsigned grid = (unsigned)std::max<size_t>(
         1, std::min<size_t>((lanes + kThreads - 1) / kThreads, (size_t)sm_count(dev) * 8));
-    softmax_lane_kernel<<<grid, kThreads, 0, s>>>(x, outer, len, inner, out);
+    softmax_lane_kernel<EXP><<<grid, kThreads, 0, s>>>(x, outer, len, inner, out);
     return cudaGetLastError();
   }
   const size_t rows = outer;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
   if (!chain && aligned && len % 4 == 0) {
-    if (len <= 512 * 2) return launch_row_reg<2>(x, rows, len, out, s);
-    if (len <= 512 * 4) return launch_row_reg<4>(x, rows, len, out, s);
-    if (len <= 512 * 8) return launch_row_reg<8>(x, rows, len, out, s);
-    if (len <= 512 * 16) return launch_row_reg<16>(x, rows, len, out, s);
+    if (len <= 512 * 2) return launch_row_reg<2, EXP>(x, rows, len, out, s);
+    if (len <= 512 * 4) return launch_row_reg<4, EXP>(x, rows, len, out, s);
+    if (len <= 512 * 8) return launch_row_reg<8, EXP>(x, rows, len, out, s);
+    if (len <= 512 * 16) return launch_row_reg<16, EXP>(x, rows, len, out, s);
   }
   if (!chain && len <= kMaxSmemRow) {
     const size_t smem = len * sizeof(float);
     if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(softmax_row_kernel,
+      cudaError_t e = cudaFuncSetAttribute(softmax_row_kernel<EXP>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }
     for (size_t r0 = 0; r0 < rows; r0 += 0x7fffffffull) {
       const size_t nr = std::min<size_t>(rows - r0, 0x7fffffffull);
-      softmax_row_kernel<<<(unsigned)nr, kRowThreads, smem, s>>>(x + r0 * len, nr, len,
+      softmax_row_kernel<EXP><<<(unsigned)nr, kRowThreads, smem, s>>>(x + r0 * len, nr, len,
                                                                  out + r0 * len);
     }
     return cudaGetLastError();
@@ -328,7 +340,7 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
     const float* xr = x + r0 * len;
     float* yr = out + r0 * len;
     row_max_kernel<<<nr, kRowThreads, 0, s>>>(xr, len, m + r0);
-    row_exp_kernel<<<dim3(gx, nr), kRowThreads, 0, s>>>(xr, len, m + r0, yr);
+    row_exp_kernel<EXP><<<dim3(gx, nr), kRowThreads, 0, s>>>(xr, len, m + r0, yr);
     if (chain)
       e = launch_lane_chain_sum(yr, nr, len, sm + r0, s);
     else
@@ -338,6 +350,14 @@ cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inne
   if (e == cudaSuccess) e = cudaGetLastError();
   const cudaError_t ef = cudaFreeAsync(scratch, s);
   return e == cudaSuccess ? ef : e;
+}
+
+}  // namespace
+
+cudaError_t launch_softmax(const float* x, size_t outer, size_t len, size_t inner,
+                           bool last_axis, float* out, cudaStream_t s) {
+  return math_exact() ? launch_softmax_exp<ExpExact>(x, outer, len, inner, last_axis, out, s)
+                      : launch_softmax_exp<ExpTol>(x, outer, len, inner, last_axis, out, s);
 }
 
 }  // namespace rt

@@ -44,3 +44,16 @@ def _built():
                 raise
             print(f"warning: rebuild skipped: {e}", file=sys.stderr)
     yield
+
+
+@pytest.fixture(scope="module")
+def exact_math():
+    """Runs a module's tests in the exact math mode (glibc's expf/tanhf
+    reproduced bit for bit) and restores the mode afterwards; the library's
+    default is the tolerance mode."""
+    from rusttorch_b200 import _native as N
+    lib = N.lib()
+    before = lib.rtc_get_math_mode()
+    N.check(lib.rtc_set_math_mode(N.MATH_EXACT))
+    yield
+    N.check(lib.rtc_set_math_mode(before))

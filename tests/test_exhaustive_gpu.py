@@ -18,7 +18,7 @@ import pytest
 
 from tests import _oracle as O
 
-pytestmark = [pytest.mark.gpu,
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_math"),
               pytest.mark.skipif(os.environ.get("RT_EXHAUSTIVE") != "1",
                                  reason="exhaustive sweep: set RT_EXHAUSTIVE=1")]
 

@@ -14,7 +14,9 @@ from rusttorch_b200 import _native as N
 from tests import _oracle as O
 from tests.test_parity_gpu import assert_bits_equal
 
-pytestmark = pytest.mark.gpu
+# Bit-exact comparisons of the transcendental activations and softmax need
+# the exact math mode (the tolerance mode is tests/test_tolerance_gpu.py).
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_math")]
 HOST = -1
 
 

@@ -21,7 +21,9 @@ import rusttorch_b200 as rt
 from rusttorch_b200 import _native as N
 from tests import _oracle as O
 
-pytestmark = pytest.mark.gpu
+# Bit-exact comparisons of the transcendental activations and softmax need
+# the exact math mode (the tolerance mode is tests/test_tolerance_gpu.py).
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_math")]
 
 NAN = np.float32(np.nan)
 
