@@ -802,22 +802,31 @@ def run_probe(args) -> None:
                 flush_rd.sum()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            call()
+            for _ in range(args.repeat):
+                call()
             e1.record(stream)
             torch.cuda.synchronize()
-            times.append(e0.elapsed_time(e1))
+            times.append(e0.elapsed_time(e1) / args.repeat)
         N.check(lib.rtc_synchronize())
         ms = statistics.median(times)
         gbs = algo_bytes / (ms * 1e-3) / 1e9
         print(json.dumps({"probe": name, "mode": mode, "p": [p0, p1, p2], "ms": ms, "GB_s": gbs,
                           "frac_of_measured_peak": gbs / peak, "bytes": algo_bytes,
-                          "l2": "dirty" if dirty else "clean"}), flush=True)
+                          "l2": "dirty" if dirty else "clean", "repeat": args.repeat}),
+              flush=True)
 
     # u < 0: the stats kernel with float32 trees per float4 (|u| loads in flight)
     for threads, u, bps in ((256, 8, 0), (512, 4, 0), (512, 8, 0), (256, -4, 0), (256, -8, 0),
                             (512, -4, 0), (512, -8, 0), (1024, -4, 0), (512, -8, 2),
-                            (256, -8, 4), (256, -8, 6), (-512, -8, 0), (-512, 8, 0)):
+                            (256, -8, 4), (256, -8, 6), (-512, -8, 0), (-512, 8, 0),
+                            (256, 2, 100), (256, 4, 100), (512, 2, 100), (512, 4, 100),
+                            (512, 2, 104), (256, 4, 108)):
         timeit(f"stats kernel t{threads} u{u} b{bps}", 7, nbytes, nbytes, threads, u, bps)
+    # cfg3's sum_dim(1): [8192, 16384]; negative: the direct-chain kernel,
+    # -(10*K + warps per CTA); 99: the bulk-copy ring kernel
+    for warps in (2, -322, 99):
+        timeit(f"lane sum [8192,16384] warps/CTA {warps}", 8, 4 * R3 * C3, 4 * R3 * C3 + 4 * R3,
+               C3, warps, 0)
     for dirty in (False, True):
         tag = "dirty-L2" if dirty else "clean-L2"
         timeit(f"{tag} cfg1 add->mul_scalar product", 5, 8 * N1, 12 * N1, 0, 4, 32, dirty)
@@ -860,6 +869,8 @@ if __name__ == "__main__":
         ap.add_argument("--probe", action="store_true")
         ap.add_argument("--steps", type=int, default=9)
         ap.add_argument("--only", default="")
+        ap.add_argument("--repeat", type=int, default=1,
+                        help="calls back to back between the events (launch gaps hidden)")
         run_probe(ap.parse_args())
     else:
         main()

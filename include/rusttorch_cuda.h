@@ -235,9 +235,10 @@ rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out);
  * a fixed array inside the library (room for 2048 partials, 32 KB per GPU,
  * held by every GPU that loads the library until exit).  The first call on a
  * device looks up that array's device address, so make it before any stream
- * capture.  Calls share the array: calls that overlap on the GPU race.
+ * capture; the address is kept, so do not use the library on a device after
+ * resetting it.  Calls share the array: calls that overlap on the GPU race.
  * Fails with RTC_INVALID_ARGUMENT if x would need more partials than the
- * array holds (only on GPUs with more than 512 SMs). */
+ * array holds (only on GPUs with more than 256 SMs). */
 rtc_result rtc_sum_device_noalloc(const rtc_tensor* x, double* device_out);
 /* sum, mean, max and min from one pass over x (no reference counterpart; each
  * value equals the corresponding single op).  out[4] = {sum, mean, max, min}. */
@@ -304,6 +305,40 @@ rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double ou
  * counterpart (the reference has no multi-device path); it is the
  * single-process form of rtc_shard_summary_local + rtc_shard_combine. */
 rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shards, double out[4]);
+
+/* More single-process sharded ops (no reference counterpart: the reference
+ * has no multi-device path; each is the sharded form of the reference export
+ * named).  A logical tensor is given as n_shards descriptors, shard i of
+ * every operand on one device (any device per shard), all f32.  Each call
+ * checks every shard before anything is launched (an argument error changes
+ * nothing), waits for the work already queued on the shards' devices, runs
+ * the shards at once (one library stream per device, launched from the
+ * calling thread) and returns when all are done.  No shard exchanges data
+ * with another: the results are those of the single-GPU op on each shard. */
+/* ops::add then ops::mul_scalar (ffi/ops.rs:21-40 rusttorch_add), any split. */
+rtc_result rtc_sharded_add_mul_scalar(const rtc_tensor* a, const rtc_tensor* b, float scalar,
+                                      const rtc_tensor* out, size_t n_shards);
+/* ops::softmax (activation.rs:92-167) of row blocks: the shards split axis 0,
+ * so dim must be >= 1 when there is more than one shard. */
+rtc_result rtc_sharded_softmax(const rtc_tensor* x, size_t dim, const rtc_tensor* out,
+                               size_t n_shards);
+/* ops::sum_dim / mean_dim (reduction.rs:75-150) and max along dim, each shard
+ * reduced on its own GPU: the shards split an axis other than dim (row blocks
+ * for the last axis; column blocks — each its own contiguous [R, C_i]
+ * tensor — for dim 0 of a matrix).  out[i] has shard i's reduced shape. */
+rtc_result rtc_sharded_sum_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out,
+                               size_t n_shards);
+rtc_result rtc_sharded_mean_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out,
+                                size_t n_shards);
+rtc_result rtc_sharded_max_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out,
+                               size_t n_shards);
+/* ops::adamw_update (optimizer.rs:379-440) on every shard, in place
+ * (params, m and v are overwritten with p', m', v'); any split. */
+rtc_result rtc_sharded_adamw_update(const rtc_tensor* params, const rtc_tensor* grads,
+                                    const rtc_tensor* m, const rtc_tensor* v,
+                                    double learning_rate, double beta1, double beta2,
+                                    double epsilon, double weight_decay, uint64_t timestep,
+                                    size_t n_shards);
 
 /* -------------------------------------------------------- broadcasting */
 /* ops::add_broadcast / sub_broadcast / mul_broadcast / div_broadcast
@@ -433,7 +468,10 @@ rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output, const rtc_t
  * wave, p2 < 0 one block per tile; 6: one balanced range per block); 7: the
  * global sum/max/min kernel over bytes/4 floats of src with p0 threads, |p1|
  * loads in flight per thread (p1 < 0: each float4 summed as a float32 tree)
- * and p2 blocks per SM (0: all that stay resident).
+ * and p2 blocks per SM (0: all that stay resident); 8: the last-axis sum of
+ * src viewed as [bytes/4/p0, p0] into dst: p1 (1, 2, 4, 8) warps per CTA of the
+ * shared-memory-staged kernel, -(10*K + w) the direct-chain kernel (K loads
+ * ahead, w warps per CTA), 99 the bulk-copy ring kernel.
  * Device pointers on the current GPU, 16-byte aligned; returns once queued. */
 rtc_result rtc_probe_stream(int mode, const void* src, void* dst, size_t bytes, int p0, int p1,
                             int p2);

@@ -29,6 +29,8 @@ __all__ = [
     "add_broadcast", "sub_broadcast", "mul_broadcast", "div_broadcast",
     "nn_adam_step", "nn_sgd_step",
     "synchronize", "set_math_mode", "get_math_mode", "math_mode",
+    "sharded_stats", "sharded_add_mul_scalar", "sharded_softmax", "sharded_sum_dim",
+    "sharded_mean_dim", "sharded_max_dim", "sharded_adamw_update",
 ]
 
 
@@ -472,3 +474,68 @@ def sharded_stats(shards) -> tuple[float, float, float, float]:
     out = (c_double * 4)()
     check(lib().rtc_sharded_stats(arr, len(shards), out))
     return out[0], out[1], out[2], out[3]
+
+
+def _desc_array(tensors):
+    arr = (_native.RtcTensor * (len(tensors) or 1))()
+    for i, t in enumerate(tensors):
+        arr[i] = t._desc.s
+    return arr
+
+
+def _like_shards(shards, shapes=None):
+    return [_like(t, shapes[i] if shapes else None) for i, t in enumerate(shards)]
+
+
+def sharded_add_mul_scalar(a, b, scalar: float):
+    """mul_scalar(add(a, b), scalar) of a tensor split into shards (lists of
+    Tensors, shard i of a and b on one GPU): one new Tensor per shard."""
+    a, b = list(a), list(b)
+    if len(a) != len(b):
+        raise ValueError("a and b must have the same number of shards")
+    out = _like_shards(a)
+    check(lib().rtc_sharded_add_mul_scalar(_desc_array(a), _desc_array(b), float(scalar),
+                                           _desc_array(out), len(a)))
+    return out
+
+
+def sharded_softmax(shards, dim: int):
+    """softmax along `dim` of row blocks (the shards split axis 0)."""
+    shards = list(shards)
+    out = _like_shards(shards)
+    check(lib().rtc_sharded_softmax(_desc_array(shards), dim, _desc_array(out), len(shards)))
+    return out
+
+
+def _sharded_dim(fn, shards, dim: int):
+    shards = list(shards)
+    dim = int(dim)
+    out = _like_shards(shards, [[d for k, d in enumerate(t.shape()) if k != dim]
+                                if 0 <= dim < t.ndim() else [] for t in shards])
+    check(fn(_desc_array(shards), dim, _desc_array(out), len(shards)))
+    return out
+
+
+def sharded_sum_dim(shards, dim: int):
+    """sum_dim of each shard on its own GPU (the shards split an axis other
+    than dim: column blocks for dim 0, row blocks for the last axis)."""
+    return _sharded_dim(lib().rtc_sharded_sum_dim, shards, dim)
+
+
+def sharded_mean_dim(shards, dim: int):
+    return _sharded_dim(lib().rtc_sharded_mean_dim, shards, dim)
+
+
+def sharded_max_dim(shards, dim: int):
+    return _sharded_dim(lib().rtc_sharded_max_dim, shards, dim)
+
+
+def sharded_adamw_update(params, grads, m, v, learning_rate, beta1, beta2, epsilon, weight_decay,
+                         timestep):
+    """adamw_update of every shard, in place (params, m, v are updated)."""
+    params, grads, m, v = list(params), list(grads), list(m), list(v)
+    if not len(params) == len(grads) == len(m) == len(v):
+        raise ValueError("params, grads, m and v must have the same number of shards")
+    check(lib().rtc_sharded_adamw_update(_desc_array(params), _desc_array(grads), _desc_array(m),
+                                         _desc_array(v), learning_rate, beta1, beta2, epsilon,
+                                         weight_decay, int(timestep), len(params)))

@@ -125,6 +125,13 @@ _SIGNATURES = {
     "rtc_shard_summary_local": (RtcResult, [T, POINTER(ShardSummary)]),
     "rtc_shard_combine": (RtcResult, [POINTER(ShardSummary), c_size_t, POINTER(c_double)]),
     "rtc_sharded_stats": (RtcResult, [POINTER(RtcTensor), c_size_t, POINTER(c_double)]),
+    "rtc_sharded_add_mul_scalar": (RtcResult, [T, T, c_float, T, c_size_t]),
+    "rtc_sharded_softmax": (RtcResult, [T, c_size_t, T, c_size_t]),
+    "rtc_sharded_sum_dim": (RtcResult, [T, c_size_t, T, c_size_t]),
+    "rtc_sharded_mean_dim": (RtcResult, [T, c_size_t, T, c_size_t]),
+    "rtc_sharded_max_dim": (RtcResult, [T, c_size_t, T, c_size_t]),
+    "rtc_sharded_adamw_update": (RtcResult, [T, T, T, T, c_double, c_double, c_double, c_double,
+                                             c_double, c_uint64, c_size_t]),
     "rtc_selftest_bounded_wait": (RtcResult, []),
     "rtc_selftest_ordered_sum": (RtcResult, [T, c_int, c_float, POINTER(c_float)]),
     "rtc_add_broadcast": (RtcResult, [T, T, T]),

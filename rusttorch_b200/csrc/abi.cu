@@ -103,6 +103,7 @@ static bool on_host(const rtc_tensor* t) { return t->device == RTC_HOST_MEMORY; 
 // ---------------------------------------------------------------- memory
 
 extern "C" rtc_result rtc_malloc(int device, size_t bytes, void** out) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   *out = nullptr;
   if (bytes == 0) return ok();
@@ -114,6 +115,7 @@ extern "C" rtc_result rtc_malloc(int device, size_t bytes, void** out) {
 }
 
 extern "C" rtc_result rtc_free(int device, void* ptr) {
+  RTC_OP_RANGE();
   if (!ptr) return ok();
   DeviceScope scope(device);
   if (!scope.ok()) return backend_error("cudaSetDevice", scope.error());
@@ -123,6 +125,7 @@ extern "C" rtc_result rtc_free(int device, void* ptr) {
 }
 
 extern "C" rtc_result rtc_memcpy_h2d(int device, void* dst, const void* src, size_t bytes) {
+  RTC_OP_RANGE();
   if (bytes == 0) return ok();
   if (!dst || !src) return invalid_argument("pointer", "must not be null");
   DeviceScope scope(device);
@@ -135,6 +138,7 @@ extern "C" rtc_result rtc_memcpy_h2d(int device, void* dst, const void* src, siz
 }
 
 extern "C" rtc_result rtc_memcpy_d2h(int device, void* dst, const void* src, size_t bytes) {
+  RTC_OP_RANGE();
   if (bytes == 0) return ok();
   if (!dst || !src) return invalid_argument("pointer", "must not be null");
   DeviceScope scope(device);
@@ -147,6 +151,7 @@ extern "C" rtc_result rtc_memcpy_d2h(int device, void* dst, const void* src, siz
 }
 
 extern "C" rtc_result rtc_host_alloc(size_t bytes, void** out) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   *out = nullptr;
   if (bytes == 0) return ok();
@@ -156,6 +161,7 @@ extern "C" rtc_result rtc_host_alloc(size_t bytes, void** out) {
 }
 
 extern "C" rtc_result rtc_host_free(void* ptr) {
+  RTC_OP_RANGE();
   if (!ptr) return ok();
   cudaError_t e = cudaFreeHost(ptr);
   if (e != cudaSuccess) return backend_error("cudaFreeHost", e);
@@ -178,11 +184,13 @@ static rtc_result fill(const rtc_tensor* out, uint64_t seed, uint64_t offset, fl
 
 extern "C" rtc_result rtc_fill_uniform(const rtc_tensor* out, uint64_t seed, uint64_t offset,
                                        float lo, float hi) {
+  RTC_OP_RANGE();
   return fill(out, seed, offset, lo, hi, 0);
 }
 
 extern "C" rtc_result rtc_fill_normal(const rtc_tensor* out, uint64_t seed, uint64_t offset,
                                       float mean, float std) {
+  RTC_OP_RANGE();
   return fill(out, seed, offset, mean, std, 1);
 }
 
@@ -223,35 +231,43 @@ static rtc_result binary(BinaryOp op, float param, const rtc_tensor* a, const rt
 }
 
 extern "C" rtc_result rtc_add(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kAdd, 0.f, a, b, out, "element-wise addition", false, nullptr);
 }
 extern "C" rtc_result rtc_mul(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kMul, 0.f, a, b, out, "element-wise multiplication", false, nullptr);
 }
 extern "C" rtc_result rtc_sub(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kSub, 0.f, a, b, out, "element-wise subtraction", false, nullptr);
 }
 extern "C" rtc_result rtc_div(const rtc_tensor* a, const rtc_tensor* b, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kDiv, 0.f, a, b, out, "element-wise division", true,
                 "Division requires floating-point tensors");
 }
 extern "C" rtc_result rtc_add_simd(const rtc_tensor* a, const rtc_tensor* b,
                                    const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kAdd, 0.f, a, b, out, "add_simd", false, nullptr);
 }
 extern "C" rtc_result rtc_mul_simd(const rtc_tensor* a, const rtc_tensor* b,
                                    const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kMul, 0.f, a, b, out, "mul_simd", false, nullptr);
 }
 // ops::add then ops::mul_scalar: add's checks apply (mul_scalar has none).
 extern "C" rtc_result rtc_add_mul_scalar(const rtc_tensor* a, const rtc_tensor* b, float scalar,
                                          const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return binary(kAddMulScalar, scalar, a, b, out, "element-wise addition", false, nullptr);
 }
 
 // simd.rs:276-297 checks shapes first, then dtypes, and needs floats (:361-366).
 extern "C" rtc_result rtc_fused_multiply_add(const rtc_tensor* a, const rtc_tensor* b,
                                              const rtc_tensor* c, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   const char* context = "fused_multiply_add";
   TRY(check_desc(a, "a"));
   TRY(check_desc(b, "b"));
@@ -319,62 +335,80 @@ static rtc_result unary(UnaryOp op, float param, const rtc_tensor* x, const rtc_
 }
 
 extern "C" rtc_result rtc_add_scalar(const rtc_tensor* x, float s, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kAddScalar, s, x, out, "add_scalar", nullptr);
 }
 extern "C" rtc_result rtc_mul_scalar(const rtc_tensor* x, float s, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kMulScalar, s, x, out, "mul_scalar", nullptr);
 }
 extern "C" rtc_result rtc_mul_scalar_simd(const rtc_tensor* x, float s, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kMulScalar, s, x, out, "mul_scalar_simd", nullptr);
 }
 extern "C" rtc_result rtc_relu(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kRelu, 0.f, x, out, "relu", nullptr);
 }
 extern "C" rtc_result rtc_relu_simd(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kRelu, 0.f, x, out, "relu_simd", nullptr);
 }
 extern "C" rtc_result rtc_leaky_relu(const rtc_tensor* x, const rtc_tensor* out, float alpha) {
+  RTC_OP_RANGE();
   return unary(kLeakyRelu, alpha, x, out, "leaky_relu", nullptr);
 }
 extern "C" rtc_result rtc_sigmoid(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kSigmoid, 0.f, x, out, "sigmoid", "Sigmoid requires floating-point tensors");
 }
 extern "C" rtc_result rtc_tanh(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kTanh, 0.f, x, out, "tanh", "Tanh requires floating-point tensors");
 }
 extern "C" rtc_result rtc_gelu(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kGelu, 0.f, x, out, "gelu", "GELU requires floating-point tensors");
 }
 extern "C" rtc_result rtc_swish(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kSwish, 0.f, x, out, "swish", "Swish requires floating-point tensors");
 }
 extern "C" rtc_result rtc_elu(const rtc_tensor* x, const rtc_tensor* out, float alpha) {
+  RTC_OP_RANGE();
   return unary(kElu, alpha, x, out, "elu", "ELU requires floating-point tensors");
 }
 extern "C" rtc_result rtc_selu(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kSelu, 0.f, x, out, "selu", "SELU requires floating-point tensors");
 }
 extern "C" rtc_result rtc_mish(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kMish, 0.f, x, out, "mish", "Mish requires floating-point tensors");
 }
 extern "C" rtc_result rtc_softplus(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kSoftplus, 0.f, x, out, "softplus", "Softplus requires floating-point tensors");
 }
 extern "C" rtc_result rtc_softsign(const rtc_tensor* x, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return unary(kSoftsign, 0.f, x, out, "softsign", "Softsign requires floating-point tensors");
 }
 
 extern "C" rtc_result rtc_relu_f32(const float* input, float* output, size_t size) {
+  RTC_OP_RANGE();
   if (size == 0) return ok();
   if (!input || !output) return invalid_argument("pointer", "must not be null");
   return launched(launch_unary(kRelu, 0.f, input, output, size, thread_stream()), "relu_f32");
 }
 extern "C" rtc_result rtc_add_f32(const float* a, const float* b, float* output, size_t size) {
+  RTC_OP_RANGE();
   if (size == 0) return ok();
   if (!a || !b || !output) return invalid_argument("pointer", "must not be null");
   return launched(launch_binary(kAdd, 0.f, a, b, output, size, thread_stream()), "add_f32");
 }
 extern "C" rtc_result rtc_mul_f32(const float* a, const float* b, float* output, size_t size) {
+  RTC_OP_RANGE();
   if (size == 0) return ok();
   if (!a || !b || !output) return invalid_argument("pointer", "must not be null");
   return launched(launch_binary(kMul, 0.f, a, b, output, size, thread_stream()), "mul_f32");
@@ -383,6 +417,7 @@ extern "C" rtc_result rtc_mul_f32(const float* a, const float* b, float* output,
 // ------------------------------------------------------------------- softmax
 
 extern "C" rtc_result rtc_softmax(const rtc_tensor* x, size_t dim, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   TRY(check_desc(x, "input"));
   TRY(check_desc(out, "out"));
   // activation.rs:93-105: float dtype first, then the dim range.
@@ -452,12 +487,15 @@ static rtc_result reduce_dim(DimReduce op, const rtc_tensor* x, size_t dim, cons
 }
 
 extern "C" rtc_result rtc_sum_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return reduce_dim(kDimSum, x, dim, out, "sum_dim");
 }
 extern "C" rtc_result rtc_mean_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return reduce_dim(kDimMean, x, dim, out, "mean_dim");
 }
 extern "C" rtc_result rtc_max_dim(const rtc_tensor* x, size_t dim, const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return reduce_dim(kDimMax, x, dim, out, "max_dim");
 }
 
@@ -492,6 +530,7 @@ static rtc_result global(const rtc_tensor* x, const char* op, bool empty_is_erro
 }
 
 extern "C" rtc_result rtc_sum(const rtc_tensor* x, double* out_value) {
+  RTC_OP_RANGE();
   if (!out_value) return invalid_argument("out_value", "must not be null");
   GlobalStats st;
   TRY(global(x, "sum", false, kStatSum, &st));
@@ -500,6 +539,7 @@ extern "C" rtc_result rtc_sum(const rtc_tensor* x, double* out_value) {
 }
 
 extern "C" rtc_result rtc_mean(const rtc_tensor* x, double* out_value) {
+  RTC_OP_RANGE();
   if (!out_value) return invalid_argument("out_value", "must not be null");
   GlobalStats st;
   TRY(global(x, "mean", true, kStatSum, &st));
@@ -508,6 +548,7 @@ extern "C" rtc_result rtc_mean(const rtc_tensor* x, double* out_value) {
 }
 
 extern "C" rtc_result rtc_max(const rtc_tensor* x, double* out_value) {
+  RTC_OP_RANGE();
   if (!out_value) return invalid_argument("out_value", "must not be null");
   GlobalStats st;
   TRY(global(x, "max", true, kStatMax, &st));
@@ -516,6 +557,7 @@ extern "C" rtc_result rtc_max(const rtc_tensor* x, double* out_value) {
 }
 
 extern "C" rtc_result rtc_min(const rtc_tensor* x, double* out_value) {
+  RTC_OP_RANGE();
   if (!out_value) return invalid_argument("out_value", "must not be null");
   GlobalStats st;
   TRY(global(x, "min", true, kStatMin, &st));
@@ -524,6 +566,7 @@ extern "C" rtc_result rtc_min(const rtc_tensor* x, double* out_value) {
 }
 
 extern "C" rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out) {
+  RTC_OP_RANGE();
   TRY(check_desc(x, "input"));
   if (!device_out) return invalid_argument("device_out", "must not be null");
   TRY(require_f32(x, "sum"));
@@ -544,6 +587,7 @@ extern "C" rtc_result rtc_sum_device(const rtc_tensor* x, double* device_out) {
 }
 
 extern "C" rtc_result rtc_stats(const rtc_tensor* x, double out[4]) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   GlobalStats st;
   TRY(global(x, "stats", true, kStatSum | kStatMax | kStatMin, &st));
@@ -557,6 +601,7 @@ extern "C" rtc_result rtc_stats(const rtc_tensor* x, double out[4]) {
 // --------------------------------------------------- sharded reductions
 
 extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard_summary* out) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   TRY(check_desc(shard, "shard"));
   rtc_shard_summary s{};
@@ -592,6 +637,7 @@ extern "C" rtc_result rtc_shard_summary_local(const rtc_tensor* shard, rtc_shard
 // devices, since the shards may come from other streams.
 extern "C" rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shards,
                                         double out[4]) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   if (n_shards > 0 && !shards) return invalid_argument("shards", "must not be null");
   for (size_t i = 0; i < n_shards; i++) TRY(check_desc(&shards[i], "shard"));
@@ -639,6 +685,7 @@ extern "C" rtc_result rtc_sharded_stats(const rtc_tensor* shards, size_t n_shard
 }
 
 extern "C" rtc_result rtc_shard_combine(const rtc_shard_summary* parts, size_t n, double out[4]) {
+  RTC_OP_RANGE();
   if (!out) return invalid_argument("out", "must not be null");
   if (n > 0 && !parts) return invalid_argument("parts", "must not be null");
   if (!combine_summaries(parts, n, out)) return empty_tensor("stats");
@@ -722,18 +769,22 @@ static rtc_result broadcast_op(BinaryOp op, const rtc_tensor* a, const rtc_tenso
 
 extern "C" rtc_result rtc_add_broadcast(const rtc_tensor* a, const rtc_tensor* b,
                                         const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return broadcast_op(kAdd, a, b, out, "element-wise addition", false, nullptr);
 }
 extern "C" rtc_result rtc_sub_broadcast(const rtc_tensor* a, const rtc_tensor* b,
                                         const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return broadcast_op(kSub, a, b, out, "element-wise subtraction", false, nullptr);
 }
 extern "C" rtc_result rtc_mul_broadcast(const rtc_tensor* a, const rtc_tensor* b,
                                         const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return broadcast_op(kMul, a, b, out, "element-wise multiplication", false, nullptr);
 }
 extern "C" rtc_result rtc_div_broadcast(const rtc_tensor* a, const rtc_tensor* b,
                                         const rtc_tensor* out) {
+  RTC_OP_RANGE();
   return broadcast_op(kDiv, a, b, out, "element-wise division", true,
                       "Division requires floating-point tensors");
 }
@@ -745,6 +796,7 @@ extern "C" rtc_result rtc_nn_adam_step(const rtc_tensor* p, const rtc_tensor* g,
                                        float beta1, float beta2, float eps, uint64_t t,
                                        const rtc_tensor* po, const rtc_tensor* mo,
                                        const rtc_tensor* vo) {
+  RTC_OP_RANGE();
   TRY(check_desc(p, "params"));
   TRY(check_desc(g, "gradients"));
   TRY(check_desc(m, "m"));
@@ -803,6 +855,7 @@ extern "C" rtc_result rtc_nn_sgd_step(const rtc_tensor* p, const rtc_tensor* g,
                                       const rtc_tensor* vel, float lr, float momentum,
                                       float weight_decay, const rtc_tensor* po,
                                       const rtc_tensor* vo) {
+  RTC_OP_RANGE();
   TRY(check_desc(p, "params"));
   TRY(check_desc(g, "gradients"));
   TRY(check_desc(po, "params_out"));
@@ -948,6 +1001,7 @@ extern "C" rtc_result rtc_adam_update(const rtc_tensor* params, const rtc_tensor
                                       double epsilon, uint64_t timestep,
                                       const rtc_tensor* params_out, const rtc_tensor* m_out,
                                       const rtc_tensor* v_out) {
+  RTC_OP_RANGE();
   return adam_common(params, grads, m, v, learning_rate, beta1, beta2, epsilon, 0.0, timestep,
                      params_out, m_out, v_out, false);
 }
@@ -958,6 +1012,7 @@ extern "C" rtc_result rtc_adamw_update(const rtc_tensor* params, const rtc_tenso
                                        double epsilon, double weight_decay, uint64_t timestep,
                                        const rtc_tensor* params_out, const rtc_tensor* m_out,
                                        const rtc_tensor* v_out) {
+  RTC_OP_RANGE();
   return adam_common(params, grads, m, v, learning_rate, beta1, beta2, epsilon, weight_decay,
                      timestep, params_out, m_out, v_out, true);
 }
@@ -965,6 +1020,7 @@ extern "C" rtc_result rtc_adamw_update(const rtc_tensor* params, const rtc_tenso
 // optimizer.rs:42-86: shape, dtype, learning rate; float only.
 extern "C" rtc_result rtc_sgd_update(const rtc_tensor* p, const rtc_tensor* g, double lr,
                                      const rtc_tensor* po) {
+  RTC_OP_RANGE();
   TRY(check_desc(p, "params"));
   TRY(check_desc(g, "gradients"));
   TRY(check_desc(po, "params_out"));
@@ -1002,6 +1058,7 @@ extern "C" rtc_result rtc_sgd_update(const rtc_tensor* p, const rtc_tensor* g, d
 extern "C" rtc_result rtc_sgd_momentum_update(const rtc_tensor* p, const rtc_tensor* g,
                                               const rtc_tensor* vel, double lr, double momentum,
                                               const rtc_tensor* po, const rtc_tensor* vo) {
+  RTC_OP_RANGE();
   TRY(check_desc(p, "params"));
   TRY(check_desc(g, "gradients"));
   TRY(check_desc(vel, "velocity"));

@@ -84,17 +84,20 @@ rtc_result grad_unary(GradUnaryOp op, const rtc_tensor* g, const rtc_tensor* sav
 
 extern "C" rtc_result rtc_relu_backward(const rtc_tensor* grad_output, const rtc_tensor* input,
                                         const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   return grad_unary(kGradRelu, grad_output, input, grad_input, "input");
 }
 
 extern "C" rtc_result rtc_sigmoid_backward(const rtc_tensor* grad_output,
                                            const rtc_tensor* output,
                                            const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   return grad_unary(kGradSigmoid, grad_output, output, grad_input, "output");
 }
 
 extern "C" rtc_result rtc_tanh_backward(const rtc_tensor* grad_output, const rtc_tensor* output,
                                         const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   return grad_unary(kGradTanh, grad_output, output, grad_input, "output");
 }
 
@@ -102,6 +105,7 @@ extern "C" rtc_result rtc_tanh_backward(const rtc_tensor* grad_output, const rtc
 // grad_output by position; the result has the input's shape.
 extern "C" rtc_result rtc_gelu_backward(const rtc_tensor* grad_output, const rtc_tensor* input,
                                         const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   const char* context = "gelu backward";
   TRY(check_desc(grad_output, "grad_output"));
   TRY(check_desc(input, "input"));
@@ -121,6 +125,7 @@ extern "C" rtc_result rtc_gelu_backward(const rtc_tensor* grad_output, const rtc
 // gelu_forward (ops.rs:3131-3141): autograd's own GELU, whose cubic term is
 // ((0.044715*x)*x)*x rather than ops::gelu's 0.044715*((x*x)*x).
 extern "C" rtc_result rtc_autograd_gelu(const rtc_tensor* input, const rtc_tensor* output) {
+  RTC_OP_RANGE();
   const char* context = "gelu_forward";
   TRY(check_desc(input, "input"));
   TRY(check_desc(output, "output"));
@@ -162,11 +167,13 @@ static rtc_result add_sub_backward(GradBinaryOp op, const rtc_tensor* g, const r
 
 extern "C" rtc_result rtc_add_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
                                        const rtc_tensor* grad_b) {
+  RTC_OP_RANGE();
   return add_sub_backward(kGradAdd, grad_output, grad_a, grad_b, "add backward");
 }
 
 extern "C" rtc_result rtc_sub_backward(const rtc_tensor* grad_output, const rtc_tensor* grad_a,
                                        const rtc_tensor* grad_b) {
+  RTC_OP_RANGE();
   return add_sub_backward(kGradSub, grad_output, grad_a, grad_b, "sub backward");
 }
 
@@ -219,12 +226,14 @@ static rtc_result mul_div_backward(GradBinaryOp op, const rtc_tensor* g, const r
 extern "C" rtc_result rtc_mul_backward(const rtc_tensor* grad_output, const rtc_tensor* a,
                                        const rtc_tensor* b, const rtc_tensor* grad_a,
                                        const rtc_tensor* grad_b) {
+  RTC_OP_RANGE();
   return mul_div_backward(kGradMul, grad_output, a, b, grad_a, grad_b);
 }
 
 extern "C" rtc_result rtc_div_backward(const rtc_tensor* grad_output, const rtc_tensor* a,
                                        const rtc_tensor* b, const rtc_tensor* grad_a,
                                        const rtc_tensor* grad_b) {
+  RTC_OP_RANGE();
   return mul_div_backward(kGradDiv, grad_output, a, b, grad_a, grad_b);
 }
 
@@ -253,11 +262,13 @@ static rtc_result fill_backward(const rtc_tensor* g, const rtc_tensor* gi, bool 
 
 extern "C" rtc_result rtc_sum_backward(const rtc_tensor* grad_output,
                                        const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   return fill_backward(grad_output, grad_input, false, "sum backward");
 }
 
 extern "C" rtc_result rtc_mean_backward(const rtc_tensor* grad_output,
                                         const rtc_tensor* grad_input) {
+  RTC_OP_RANGE();
   return fill_backward(grad_output, grad_input, true, "mean backward");
 }
 
@@ -307,6 +318,7 @@ static rtc_result reduce_to_shape(const rtc_tensor* g, const rtc_tensor* o, cuda
 extern "C" rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output,
                                                  const rtc_tensor* grad_a,
                                                  const rtc_tensor* grad_b) {
+  RTC_OP_RANGE();
   const char* context = "broadcast_add backward";
   TRY(check_desc(grad_output, "grad_output"));
   if (grad_a) TRY(check_desc(grad_a, "grad_a"));

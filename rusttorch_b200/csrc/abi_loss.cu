@@ -63,6 +63,7 @@ rtc_result run_loss(LossOp op, const rtc_tensor* p, const rtc_tensor* t, float a
 
 extern "C" rtc_result rtc_mse_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
                                    double* out_value) {
+  RTC_OP_RANGE();
   const char* ctx = "mse_loss";
   if (!out_value) return invalid_argument("out_value", "must not be null");
   TRY(shape_dtype(predictions, targets, ctx, true));
@@ -73,6 +74,7 @@ extern "C" rtc_result rtc_mse_loss(const rtc_tensor* predictions, const rtc_tens
 
 extern "C" rtc_result rtc_l1_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
                                   double* out_value) {
+  RTC_OP_RANGE();
   const char* ctx = "l1_loss";
   if (!out_value) return invalid_argument("out_value", "must not be null");
   TRY(shape_dtype(predictions, targets, ctx, true));
@@ -84,6 +86,7 @@ extern "C" rtc_result rtc_l1_loss(const rtc_tensor* predictions, const rtc_tenso
 // loss.rs:182-188: `beta <= 0.0` (a NaN beta passes)
 extern "C" rtc_result rtc_smooth_l1_loss(const rtc_tensor* predictions, const rtc_tensor* targets,
                                          double beta, double* out_value) {
+  RTC_OP_RANGE();
   const char* ctx = "smooth_l1_loss";
   if (!out_value) return invalid_argument("out_value", "must not be null");
   TRY(shape_dtype(predictions, targets, ctx, true));
@@ -113,12 +116,14 @@ static rtc_result xent(LossOp op, const rtc_tensor* p, const rtc_tensor* t, doub
 extern "C" rtc_result rtc_binary_cross_entropy_loss(const rtc_tensor* predictions,
                                                     const rtc_tensor* targets, double epsilon,
                                                     double* out_value) {
+  RTC_OP_RANGE();
   return xent(kLossBce, predictions, targets, epsilon, "binary_cross_entropy_loss", out_value);
 }
 
 extern "C" rtc_result rtc_cross_entropy_loss(const rtc_tensor* predictions,
                                              const rtc_tensor* targets, double epsilon,
                                              double* out_value) {
+  RTC_OP_RANGE();
   return xent(kLossCe, predictions, targets, epsilon, "cross_entropy_loss", out_value);
 }
 
@@ -127,6 +132,7 @@ extern "C" rtc_result rtc_cross_entropy_loss(const rtc_tensor* predictions,
 // + ... for chains == 1 — the sums that the losses above reproduce.
 extern "C" rtc_result rtc_selftest_ordered_sum(const rtc_tensor* x, int chains, float init,
                                                float* out_value) {
+  RTC_OP_RANGE();
   const char* ctx = "selftest_ordered_sum";
   if (!out_value) return invalid_argument("out_value", "must not be null");
   TRY(check_desc(x, "x"));

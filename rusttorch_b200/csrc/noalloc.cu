@@ -23,16 +23,19 @@
 namespace rt {
 namespace {
 
-// Room for this many per-block partials.  The reduction uses at most four
-// blocks per SM (stats_max_parts), so 2048 covers any GPU with up to 512 SMs;
-// B200 uses 592.
+// Room for this many per-block partials.  The reduction launches at most
+// eight blocks per SM (stats_max_parts), so 2048 covers any GPU with up to
+// 256 SMs; B200 uses 1184.
 constexpr int kNoAllocMaxParts = 2048;
 
 static __device__ __align__(256) StatsPart g_noalloc_parts[kNoAllocMaxParts];
 
 // Device address of g_noalloc_parts per device.  In host code the symbol's
 // name is only a host-side stand-in, so the address is looked up once per
-// device with that device current.
+// device with that device current, on the first call there, and kept.  A
+// device reset (cudaDeviceReset, or the primary context reset by the host
+// application) invalidates it: the library must not be used on a device
+// after that device has been reset.
 std::mutex g_mu;
 std::vector<StatsPart*> g_addr;
 
@@ -55,6 +58,7 @@ cudaError_t scratch_address(int device, StatsPart** out) {
 using namespace rt;
 
 extern "C" rtc_result rtc_sum_device_noalloc(const rtc_tensor* x, double* device_out) {
+  RTC_OP_RANGE();
   TRY(check_desc(x, "input"));
   if (!device_out) return invalid_argument("device_out", "must not be null");
   TRY(require_f32(x, "sum"));

@@ -21,9 +21,13 @@
 //          a = src, b = src + bytes/2 (bytes/2 each), out = dst.
 //  mode 6  the same map with one contiguous balanced range per block,
 //          p2 blocks per SM (0: one wave).
+//  mode 8  the last-axis sum of src viewed as [bytes/4/p0, p0] (cfg3's
+//          sum_dim(1) for p0 = 16384) into dst by the four-lanes-per-warp
+//          kernel with p1 warps per CTA.
 //  mode 7  the global sum/max/min kernel (reduce.cu) in the shape p0
 //          threads, p1 loads in flight per thread, p2 blocks per SM (0: as
-//          many as stay resident), over bytes/4 floats of src.
+//          many as stay resident), over bytes/4 floats of src; p2 >= 100:
+//          the grid-stride pipelined kernel with p2 - 100 blocks per SM.
 //
 // Every mbarrier wait is bounded (rt_tma.cuh); a ring that gives up raises
 // the library's wait-timeout flag (reported by rtc_synchronize), waits
@@ -87,15 +91,6 @@ __global__ void probe_copy_kernel(const float4* x, float4* y, size_t n4) {
   for (; i < n4; i += stride) __stcs(y + i, __ldcs(x + i));
 }
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 constexpr int kRingThreads = 256;
 constexpr int kMaxSlots = 16;
 
@@ -147,7 +142,7 @@ probe_ring_kernel(const char* src, size_t nchunks, unsigned chunk, int slots, fl
       __syncthreads();
     }
     if (tid == 0 && c + slots < c1) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_proxy_async_smem();
       mbar_arrive_expect_tx(&full[s], chunk);
       bulk_load(smem + (size_t)s * chunk, src + (c + slots) * chunk, chunk, &full[s]);
     }
@@ -275,12 +270,20 @@ cudaError_t launch_probe(int mode, const void* src, void* dst, size_t bytes, int
       default: return cudaErrorInvalidValue;
     }
   }
+  if (mode == 8) {
+    if (p0 <= 0 || bytes % (4 * (size_t)p0) != 0) return cudaErrorInvalidValue;
+    return launch_lane_sum_variant(p1, static_cast<const float*>(src), bytes / 4 / p0, (size_t)p0,
+                                   static_cast<float*>(dst), s);
+  }
   if (mode == 7) {
     StatsPart* parts = nullptr;
     double* sum = nullptr;
     e = cudaGetSymbolAddress((void**)&parts, g_probe_parts);
     if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&sum, g_probe_sum);
     if (e != cudaSuccess) return e;
+    if (p2 >= 100)   // the grid-stride pipelined kernel, p2 - 100 blocks per SM
+      return launch_stats_gs_variant(p0, p1, p2 - 100, static_cast<const float*>(src), bytes / 4,
+                                     parts, kProbeParts, s, sum);
     return launch_stats_variant(p0, p1, p2, static_cast<const float*>(src), bytes / 4, parts,
                                 kProbeParts, s, sum);
   }
@@ -310,6 +313,7 @@ __global__ void fastmath_kernel(int which, const float* x, float* out, size_t n)
 using namespace rt;
 
 extern "C" rtc_result rtc_selftest_fastmath(int which, const float* x, float* out, size_t n) {
+  RTC_OP_RANGE();
   if (which < 0 || which > 3) return invalid_argument("which", "must be 0..3");
   if (n == 0) return ok();
   if (!x || !out) return invalid_argument("x/out", "must not be null");
@@ -320,8 +324,9 @@ extern "C" rtc_result rtc_selftest_fastmath(int which, const float* x, float* ou
 
 extern "C" rtc_result rtc_probe_stream(int mode, const void* src, void* dst, size_t bytes,
                                        int p0, int p1, int p2) {
+  RTC_OP_RANGE();
   if (!src) return invalid_argument("src", "must not be null");
-  if ((mode == 4 || mode == 5 || mode == 6) && !dst)
+  if ((mode == 4 || mode == 5 || mode == 6 || mode == 8) && !dst)
     return invalid_argument("dst", "must not be null");
   if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u)
     return invalid_argument("src/dst", "must be 16-byte aligned");

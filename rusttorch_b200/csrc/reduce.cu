@@ -187,6 +187,65 @@ stats_kernel(const float* x, size_t n, size_t chunk, StatsPart* parts) {
   if (threadIdx.x == 0) parts[blockIdx.x] = StatsPart{a.s, a.mx, a.mn};
 }
 
+// The same statistics with the loads interleaved over the whole grid (block
+// b, thread t reads float4 b*NT + t, then every gridDim*NT further, as one
+// sweep of all SMs through the tensor) and software-pipelined: the next U
+// loads are issued before the current U are reduced.  Block 0 also takes
+// the unaligned head and the tail.
+template <int NT, int U>
+__global__ void __launch_bounds__(NT)
+stats_gs_kernel(const float* x, size_t n, StatsPart* parts) {
+  Acc a;
+  a.init();
+  double s1 = 0.0;
+  size_t head = ((16u - (reinterpret_cast<uintptr_t>(x) & 15u)) & 15u) >> 2;
+  if (head > n) head = n;
+  const float4* q = reinterpret_cast<const float4*>(x + head);
+  const size_t n4 = (n - head) >> 2;
+  if (blockIdx.x == 0) {
+    if (threadIdx.x < head) a.add(__ldcs(x + threadIdx.x));
+    const size_t done = head + (n4 << 2);
+    if (threadIdx.x < n - done) a.add(__ldcs(x + done + threadIdx.x));
+  }
+  const size_t stride = (size_t)gridDim.x * NT;
+  size_t i = (size_t)blockIdx.x * NT + threadIdx.x;
+  auto reduce = [&](const float4* v) {
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const double t = sum4<true>(v[u]);
+      if (u & 1) s1 = dadd(s1, t);
+      else a.s = dadd(a.s, t);
+      a.mx = fmax3(fmax3(a.mx, v[u].x, v[u].y), v[u].z, v[u].w);
+      a.mn = fmin3(fmin3(a.mn, v[u].x, v[u].y), v[u].z, v[u].w);
+    }
+  };
+  if (i + (U - 1) * stride < n4) {
+    float4 cur[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) cur[u] = __ldcs(q + i + u * stride);
+    for (; i + (2 * U - 1) * stride < n4; i += U * stride) {
+      float4 nxt[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) nxt[u] = __ldcs(q + i + (U + u) * stride);
+      reduce(cur);
+#pragma unroll
+      for (int u = 0; u < U; u++) cur[u] = nxt[u];
+    }
+    reduce(cur);
+    i += U * stride;
+  }
+  for (; i < n4; i += stride) {
+    const float4 v = __ldcs(q + i);
+    a.add(v.x);
+    a.add(v.y);
+    a.add(v.z);
+    a.add(v.w);
+  }
+  a.s = dadd(a.s, s1);
+  block_reduce<NT>(a);
+  if (threadIdx.x == 0) parts[blockIdx.x] = StatsPart{a.s, a.mx, a.mn};
+}
+
 __global__ void __launch_bounds__(kStatsThreads)
 stats_final_kernel(const StatsPart* parts, int nparts, StatsPart* out, double* sum_out) {
   Acc a;
@@ -608,16 +667,20 @@ __global__ void div_by_len_kernel(float* out, size_t lanes, size_t len) {
 // next kLqAhead tiles' 16-byte loads in flight in registers.  Only
 // __syncwarp couples the threads.  Needs len % 4 == 0 and a 16-byte-aligned
 // base.
-constexpr int kLqWarps = 8;
+// WARPS warps per CTA: small CTAs spread the warps evenly over the SMs (with
+// 8-warp CTAs, cfg3's 256 CTAs put two on 108 SMs and one on the other 40,
+// and the kernel waits for the busier SMs).
+constexpr int kLqWarps = 2;
 constexpr int kLqTile = 128;     // floats of each row per tile step
 constexpr int kLqPitch = kLqTile + 8;
 constexpr int kLqAhead = 4;
 
-__global__ void __launch_bounds__(kLqWarps * 32)
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
 lane_sum8_quad_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
-  __shared__ __align__(16) float tile_buf[kLqWarps][4 * kLqPitch];
+  __shared__ __align__(16) float tile_buf[WARPS][4 * kLqPitch];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t r0 = ((size_t)blockIdx.x * kLqWarps + warp) * 4;
+  const size_t r0 = ((size_t)blockIdx.x * WARPS + warp) * 4;
   if (r0 >= lanes) return;                             // whole warp leaves together
   float* buf = tile_buf[warp];
   const size_t steps = len / 8;                        // chain steps per row
@@ -668,6 +731,99 @@ lane_sum8_quad_kernel(const float* x, size_t lanes, size_t len, float* out, int 
     if (mean) acc = fdiv(acc, (float)len);
     out[row] = acc;
   }
+}
+
+// ------------------------------------------ last-axis sum, chains read directly
+// The same eight chains per row as above, four rows per warp, each thread
+// running one chain (thread 8r + j: chain j of the warp's row r), but every
+// chain reads its own floats straight from global memory with 4-byte loads
+// (x[8k + j] for k = 0, 1, ...): the eight threads of a row read 32
+// consecutive bytes, one full sector, so no byte is fetched twice and nothing
+// passes through shared memory.  K loads per thread are in flight while the
+// previous K are added (double-buffered registers), ~2 instructions per
+// element instead of the staged kernel's ~13; any alignment, any len >= 8.
+template <int WARPS, int K>
+__global__ void __launch_bounds__(WARPS * 32)
+lane_sum8_direct_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t r0 = ((size_t)blockIdx.x * WARPS + warp) * 4;
+  if (r0 >= lanes) return;                             // whole warp leaves together
+  const int rr = lane >> 3, j = lane & 7;
+  const size_t row = r0 + rr;
+  const bool live = row < lanes;
+  const float* xr = x + (live ? row : r0) * len;       // idle lanes reread row r0
+  const float* p = xr + j;
+  const size_t steps = len / 8;                        // chain steps per row
+  float acc = 0.0f;
+  size_t k = 0;
+  if (steps >= (size_t)K) {
+    float cur[K];
+#pragma unroll
+    for (int u = 0; u < K; u++) cur[u] = __ldcs(p + 8 * u);
+    p += 8 * K;
+    for (k = K; k + K <= steps; k += K) {
+      float nxt[K];
+#pragma unroll
+      for (int u = 0; u < K; u++) nxt[u] = __ldcs(p + 8 * u);
+      p += 8 * K;
+#pragma unroll
+      for (int u = 0; u < K; u++) acc = fadd(acc, cur[u]);
+#pragma unroll
+      for (int u = 0; u < K; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < K; u++) acc = fadd(acc, cur[u]);
+  }
+  for (; k < steps; k++, p += 8) acc = fadd(acc, __ldcs(p));
+  float q[8];
+#pragma unroll
+  for (int t = 0; t < 8; t++) q[t] = __shfl_sync(0xffffffffu, acc, (lane & ~7) + t);
+  if (j == 0 && live) {
+    float r = 0.0f;
+    r = fadd(r, fadd(q[0], q[4]));
+    r = fadd(r, fadd(q[1], q[5]));
+    r = fadd(r, fadd(q[2], q[6]));
+    r = fadd(r, fadd(q[3], q[7]));
+    for (size_t t = steps * 8; t < len; t++) r = fadd(r, xr[t]);
+    if (mean) r = fdiv(r, (float)len);
+    out[row] = r;
+  }
+}
+
+template <int WARPS, int K>
+void launch_lane_direct_w(const float* x, size_t lanes, size_t len, float* out, bool mean,
+                          cudaStream_t s) {
+  const size_t per_cta = (size_t)WARPS * 4;      // rows
+  const size_t grid = (lanes + per_cta - 1) / per_cta;
+  for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+    const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+    lane_sum8_direct_kernel<WARPS, K><<<(unsigned)ng, WARPS * 32, 0, s>>>(
+        x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta, mean);
+  }
+}
+
+template <int WARPS>
+void launch_lane_quad_w(const float* x, size_t lanes, size_t len, float* out, bool mean,
+                        cudaStream_t s) {
+  const size_t per_cta = (size_t)WARPS * 4;      // rows
+  const size_t grid = (lanes + per_cta - 1) / per_cta;
+  for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+    const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+    lane_sum8_quad_kernel<WARPS><<<(unsigned)ng, WARPS * 32, 0, s>>>(
+        x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta, mean);
+  }
+}
+
+cudaError_t launch_lane_quad(int warps, const float* x, size_t lanes, size_t len, float* out,
+                             bool mean, cudaStream_t s) {
+  switch (warps) {
+    case 1: launch_lane_quad_w<1>(x, lanes, len, out, mean, s); break;
+    case 2: launch_lane_quad_w<2>(x, lanes, len, out, mean, s); break;
+    case 4: launch_lane_quad_w<4>(x, lanes, len, out, mean, s); break;
+    case 8: launch_lane_quad_w<8>(x, lanes, len, out, mean, s); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 // Any layout: one thread per output, sequential over len (row order).
@@ -727,14 +883,12 @@ cudaError_t strip_launch(const float* x, size_t outer, size_t len, size_t inner,
   return cudaGetLastError();
 }
 
-// The stats kernel's shape: threads per block, loads in flight per thread,
-// and the blocks per SM that stay resident together (so that one wave of
-// blocks covers the tensor and every block streams the same number of bytes).
-struct StatsShape {
-  int threads, u;
-  bool f32tree;
-};
-constexpr StatsShape kStatsShape{512, 8, true};
+// The global statistics run stats_gs_kernel<256, 4> with 8 blocks per SM
+// (more than stay resident at once; the grid stride keeps every block's
+// share equal): 0.99-1.00 of the measured copy bandwidth at cfg2, where the
+// one-contiguous-range-per-block stats_kernel reached 0.86-0.89 in every
+// shape (bench.py --probe).
+constexpr int kStatsGsThreads = 256, kStatsGsU = 4, kStatsGsBlocksPerSm = 8;
 
 template <int NT, int U, bool T>
 int stats_resident(int device) {
@@ -762,22 +916,44 @@ cudaError_t launch_stats_shape(const float* x, size_t n, StatsPart* parts, int n
 
 }  // namespace
 
-int stats_max_parts(int device) {
-  return sm_count(device) *
-         stats_resident<kStatsShape.threads, kStatsShape.u, kStatsShape.f32tree>(device);
-}
+int stats_max_parts(int device) { return sm_count(device) * kStatsGsBlocksPerSm; }
 
 int stats_num_parts(int device, size_t n) {
-  // At least ~16K elements per block so that small inputs use few blocks;
-  // at most one resident wave.
+  // At least ~16K elements per block so that small inputs use few blocks.
   const size_t want = (n + 16383) / 16384;
   return (int)std::max<size_t>(1, std::min<size_t>(want, (size_t)stats_max_parts(device)));
 }
 
 cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts, StatsPart* out,
                          cudaStream_t s, double* sum_out) {
-  return launch_stats_shape<kStatsShape.threads, kStatsShape.u, kStatsShape.f32tree>(
-      x, n, parts, nparts, out, s, sum_out);
+  stats_gs_kernel<kStatsGsThreads, kStatsGsU><<<nparts, kStatsGsThreads, 0, s>>>(x, n, parts);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, nparts, out, sum_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lane_sum_variant(int warps, const float* x, size_t lanes, size_t len,
+                                    float* out, cudaStream_t s) {
+  if (warps == 99) {   // the bulk-copy ring kernel
+    bool used = false;
+    const cudaError_t e = launch_lane_sum_bulk(x, lanes, len, out, false, s, &used);
+    return used ? e : cudaErrorInvalidValue;
+  }
+  // warps < 0: the direct kernel with -warps = 10*K + warps per CTA (K = 16, 32)
+  if (warps < 0) {
+    const int code = -warps, K = code / 10, w = code % 10;
+    if (len < 8) return cudaErrorInvalidValue;
+    if (K == 16 && w == 2) launch_lane_direct_w<2, 16>(x, lanes, len, out, false, s);
+    else if (K == 32 && w == 1) launch_lane_direct_w<1, 32>(x, lanes, len, out, false, s);
+    else if (K == 32 && w == 2) launch_lane_direct_w<2, 32>(x, lanes, len, out, false, s);
+    else if (K == 32 && w == 4) launch_lane_direct_w<4, 32>(x, lanes, len, out, false, s);
+    else if (K == 64 && w == 2) launch_lane_direct_w<2, 64>(x, lanes, len, out, false, s);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+  }
+  if (len % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return cudaErrorInvalidValue;
+  return launch_lane_quad(warps, x, lanes, len, out, false, s);
 }
 
 cudaError_t launch_stats_variant(int threads, int u, int blocks_per_sm, const float* x, size_t n,
@@ -810,6 +986,34 @@ cudaError_t launch_stats_variant(int threads, int u, int blocks_per_sm, const fl
   return cudaErrorInvalidValue;
 }
 
+// The grid-stride, pipelined kernel: `threads` 256/512, `u` 2/4, blocks per
+// SM as given (0: all that stay resident).
+cudaError_t launch_stats_gs_variant(int threads, int u, int blocks_per_sm, const float* x,
+                                    size_t n, StatsPart* parts, int max_parts, cudaStream_t s,
+                                    double* sum_out) {
+  const int dev = cur_device();
+#define RT_STATS_GS(NT, UU)                                                                 \
+  if (threads == NT && u == UU) {                                                           \
+    int per = blocks_per_sm;                                                                \
+    if (per <= 0 &&                                                                         \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, stats_gs_kernel<NT, UU>, NT, 0) != \
+            cudaSuccess)                                                                    \
+      per = 1;                                                                              \
+    const int np = std::max(1, std::min(per * sm_count(dev), max_parts));                   \
+    stats_gs_kernel<NT, UU><<<np, NT, 0, s>>>(x, n, parts);                                 \
+    cudaError_t e = cudaGetLastError();                                                     \
+    if (e != cudaSuccess) return e;                                                         \
+    stats_final_kernel<<<1, kStatsThreads, 0, s>>>(parts, np, nullptr, sum_out);            \
+    return cudaGetLastError();                                                              \
+  }
+  RT_STATS_GS(256, 2)
+  RT_STATS_GS(256, 4)
+  RT_STATS_GS(512, 2)
+  RT_STATS_GS(512, 4)
+#undef RT_STATS_GS
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_index_scan(const float* x, size_t n, IndexScan* out, cudaStream_t s) {
   index_scan_init<<<1, 1, 0, s>>>(out);
   const size_t want = (n + kThreads - 1) / kThreads;
@@ -829,18 +1033,17 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     if (op == kDimMax) {
       const unsigned grid = (unsigned)((lanes + 7) / 8);
       lane_max_kernel<<<grid, kWarpLaneThreads, 0, s>>>(x, lanes, len, out);
-    } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 1024 &&
-               lanes >= (size_t)sm_count(cur_device()) * 28) {
-      // enough lanes for ~28 warps per SM (fewer leave the warp kernel
-      // under-occupied; the staged kernel below spreads 4 lanes per CTA)
-      const size_t per_cta = (size_t)kLqWarps * 4;      // rows
-      const size_t grid = (lanes + per_cta - 1) / per_cta;
-      for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
-        const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
-        lane_sum8_quad_kernel<<<(unsigned)ng, kLqWarps * 32, 0, s>>>(
-            x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta,
-            op == kDimMean);
-      }
+    } else if (len >= 1024 && lanes >= (size_t)sm_count(cur_device()) * 28) {
+      // enough lanes for ~7 warps per SM (fewer leave the warp kernel
+      // under-occupied; the staged kernel below spreads 4 lanes per CTA):
+      // rows through a cp.async.bulk ring when they are 16-byte aligned
+      // (lane_bulk.cu), else the chains read straight from global memory
+      // (0.795 of the measured bandwidth at cfg3 against 0.737 for the
+      // shared-memory-staged lane_sum8_quad_kernel, bench.py --probe)
+      bool used = false;
+      const cudaError_t e = launch_lane_sum_bulk(x, lanes, len, out, op == kDimMean, s, &used);
+      if (e != cudaSuccess) return e;
+      if (!used) launch_lane_direct_w<2, 32>(x, lanes, len, out, op == kDimMean, s);
     } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
       const size_t grid = (lanes + kLsRows - 1) / kLsRows;
       // deepest ring whose CTAs are all resident in one wave (else 4)

@@ -259,7 +259,16 @@ void keep_pool_memory(int device) {
   g_pool_set[device] = true;
 }
 
+bool nvtx_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("RTC_NVTX");
+    return v && std::strcmp(v, "1") == 0;
+  }();
+  return on;
+}
+
 void release_library_state() {
+  release_sharded_streams();
   std::lock_guard<std::mutex> lock(g_pool_mu);
   for (size_t d = 0; d < g_pool_set.size(); d++) {
     if (!g_pool_set[d]) continue;

@@ -5,6 +5,8 @@
 #include "../../include/rusttorch_cuda.h"
 #include "rt_internal.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <string>
 #include <vector>
 
@@ -41,6 +43,25 @@ std::string rust_f64(double v);
 std::string dtype_debug(int dtype);
 std::string dtype_display(int dtype);
 
+// ---- tracing ----------------------------------------------------------------
+// An NVTX range named after the C-ABI entry point around each op call, when
+// the environment variable RTC_NVTX is 1 at the first call (otherwise one
+// load and branch).  Profilers that record NVTX (ncu --nvtx, nsys) then show
+// which op every kernel belongs to.  NVTX is header-only: nothing is linked.
+bool nvtx_enabled();
+struct OpRange {
+  bool on;
+  explicit OpRange(const char* name) : on(nvtx_enabled()) {
+    if (on) nvtxRangePushA(name);
+  }
+  ~OpRange() {
+    if (on) nvtxRangePop();
+  }
+  OpRange(const OpRange&) = delete;
+  OpRange& operator=(const OpRange&) = delete;
+};
+#define RTC_OP_RANGE() ::rt::OpRange rtc_op_range_(__func__)
+
 // ---- descriptors ------------------------------------------------------------
 rtc_result check_desc(const rtc_tensor* t, const char* name);   // structural sanity
 bool is_float(int dtype);
@@ -76,6 +97,8 @@ void set_thread_stream(cudaStream_t s);
 // (scratch of the reductions is allocated per call with cudaMallocAsync).
 void keep_pool_memory(int device);
 void release_library_state();
+// Destroys the per-device streams of the sharded entry points (abi_sharded.cu).
+void release_sharded_streams();
 
 // ---- exact global statistics ------------------------------------------------
 // Sum (f64) and the reference's max/min fold results of x[0..n), n > 0.

@@ -24,8 +24,8 @@
 //    plus k*ln2 in two parts;
 //  * reciprocal — the hardware approximation refined by two Newton-Raphson
 //    steps y' = y + y*(1 - d*y) (fused), which is the correctly rounded 1/d
-//    for every d in [1, 2^64] (tests/test_fastmath_gpu.py checks it against
-//    IEEE division on the device); the host build divides.
+//    for every d in [1, 2^64] (rcp_rn in rt_libm.cuh; tests/test_tolerance_gpu.py
+//    checks it against IEEE division on the device); the host build divides.
 #pragma once
 
 #include "rt_libm.cuh"
@@ -42,19 +42,8 @@ RT_HD float ffma(float a, float b, float c) {
 
 RT_HD float fabs_bits(float x) { return u2f(f2u(x) & 0x7fffffffu); }
 
-// 1/d rounded to nearest for d in [1, 2^64] (and NaN for NaN).
-RT_HD float rcp_cr(float d) {
-#if defined(__CUDA_ARCH__)
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
-  float e = __fmaf_rn(-d, y, 1.0f);
-  y = __fmaf_rn(y, e, y);
-  e = __fmaf_rn(-d, y, 1.0f);
-  return __fmaf_rn(y, e, y);
-#else
-  return 1.0f / d;
-#endif
-}
+// 1/d rounded to nearest for d in [1, 2^64] (and NaN for NaN): rcp_rn.
+RT_HD float rcp_cr(float d) { return rcp_rn(d); }
 
 // e^x = p * s1 * s2 for x in [-104, 89] (or NaN): p in [0.70, 1.42] and s1,
 // s2 powers of two (each in [2^-75, 2^64]).  Callers that scale the result
@@ -119,6 +108,18 @@ RT_HD float tanh_fast(float x) {
   const float big = ffma(-2.0f, rcp_cr(fadd(fmul(fmul(e.p, e.s1), e.s2), 1.0f)), 1.0f);
   const float r = ax < 0.55f ? small : big;
   return u2f(f2u(r) | sign);
+}
+
+// tanh(z) to within a few units of 2^-24 in ABSOLUTE terms, which is all
+// GELU needs of it above its exact range (it only uses 1 + tanh(z), which is
+// above 0.1 there): tanh_fast's large-|z| formula 1 - 2/(e^(2|z|) + 1) on
+// every input, so no small-|z| polynomial; near 0 its cancellation costs
+// relative accuracy of tanh itself, not absolute.
+RT_HD float tanh_fast_abs(float z) {
+  const float az = fabs_bits(z);
+  const ExpParts e = exp_parts(fmul(2.0f, az > 9.5f ? 9.5f : az));
+  const float t = ffma(-2.0f, rcp_cr(fadd(fmul(fmul(e.p, e.s1), e.s2), 1.0f)), 1.0f);
+  return u2f(f2u(t) | (f2u(z) & 0x80000000u));
 }
 
 // log(y) for a positive normal finite y (or NaN).

@@ -105,6 +105,23 @@ cudaError_t launch_stats_variant(int threads, int u, int blocks_per_sm, const fl
                                  StatsPart* parts, int max_parts, cudaStream_t s,
                                  double* sum_out);
 
+// The grid-stride, software-pipelined stats kernel (threads 256/512, u 2/4).
+cudaError_t launch_stats_gs_variant(int threads, int u, int blocks_per_sm, const float* x,
+                                    size_t n, StatsPart* parts, int max_parts, cudaStream_t s,
+                                    double* sum_out);
+
+// The last-axis sum (mean) of [lanes, len] through a cp.async.bulk ring
+// (lane_bulk.cu); *used = false (nothing launched) when the layout does not
+// suit it (unaligned rows, len < 1024).
+cudaError_t launch_lane_sum_bulk(const float* x, size_t lanes, size_t len, float* out, bool mean,
+                                 cudaStream_t s, bool* used);
+
+// The last-axis sum of [lanes, len] (len % 4 == 0, 16-byte-aligned x) by
+// the four-lanes-per-warp kernel with `warps` (1, 2, 4, 8) warps per CTA.
+// For the probes.
+cudaError_t launch_lane_sum_variant(int warps, const float* x, size_t lanes, size_t len,
+                                    float* out, cudaStream_t s);
+
 // Positions used by the exact repair path, 1-based (0 = none).
 struct IndexScan {
   unsigned long long last_nan;    // last i+1 with x[i] NaN

@@ -33,6 +33,29 @@
 // Device code must keep one rounding per f32 operation: this header uses the
 // explicit _rn intrinsics on the device, and plain operators on the host (the
 // host build of the checker uses -ffp-contract=off).
+//
+// Third-party notices for the constants and steps restated here:
+//
+//  * expm1f / tanhf follow fdlibm's single-precision functions, whose notice
+//    reads:
+//      Copyright (C) 1993 by Sun Microsystems, Inc. All rights reserved.
+//      Developed at SunPro, a Sun Microsystems, Inc. business.
+//      Permission to use, copy, modify, and distribute this
+//      software is freely granted, provided that this notice
+//      is preserved.
+//    (float conversion by Ian Lance Taylor, Cygnus Support.)
+//  * expf follows the method and constants of Arm's optimized-routines
+//    (Szabolcs Nagy), Copyright (c) 2017-2018 Arm Limited, distributed under
+//    the MIT License (SPDX-License-Identifier: MIT OR Apache-2.0 WITH
+//    LLVM-exception), which requires this notice to be kept:
+//      Permission is hereby granted, free of charge, to any person obtaining
+//      a copy of this software and associated documentation files, to deal
+//      in the Software without restriction, subject to the following
+//      condition: the above copyright notice and this permission notice
+//      shall be included in all copies or substantial portions of the
+//      Software.  THE SOFTWARE IS PROVIDED "AS IS", WITHOUT WARRANTY OF ANY
+//      KIND.
+//    The 2^(i/32) table is recomputed here, not copied.
 #pragma once
 
 #include <stdint.h>
@@ -374,6 +397,85 @@ RT_HD float tanhf_common(float x) {
   // tanh = 1 - 2/(t+2) for |x| >= 1, -t/(t+2) below: one division.
   const float q = fdiv(ge1 ? 2.0f : -t, fadd(t, 2.0f));
   const float z = ge1 ? fsub(1.0f, q) : q;
+  return (f2u(x) >> 31) ? -z : z;
+}
+
+// The correctly rounded reciprocal of d in [1, 2^64]: the device refines
+// the hardware approximation by two Newton-Raphson steps y' = y + y(1 - d*y)
+// (fused), which tests/test_tolerance_gpu.py checks against IEEE division;
+// the host divides.
+RT_HD float rcp_rn(float d) {
+#if defined(__CUDA_ARCH__)
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+  float e = __fmaf_rn(-d, y, 1.0f);
+  y = __fmaf_rn(y, e, y);
+  e = __fmaf_rn(-d, y, 1.0f);
+  return __fmaf_rn(y, e, y);
+#else
+  return 1.0f / d;
+#endif
+}
+
+// n/d rounded to nearest, for normal n and d with d in [1, 2^64] and a
+// normal quotient: Markstein's correction of q = n*y by the residual
+// r = n - d*q (exact in one fused multiply-add), q' = q + r*y with y the
+// correctly rounded 1/d, gives the correctly rounded quotient (Markstein,
+// "IA-64 and Elementary Functions", 2000, Theorem 8.10).
+RT_HD float fdiv_markstein(float n, float d) {
+  const float y = rcp_rn(d);
+#if defined(__CUDA_ARCH__)
+  const float q = __fmul_rn(n, y);
+  const float r = __fmaf_rn(-d, q, n);
+  return __fmaf_rn(r, y, q);
+#else
+  const float q = n * y;
+  const float r = fmaf(-d, q, n);
+  return fmaf(r, y, q);
+#endif
+}
+
+// tanhf for 1 <= |x| < 22 only (GELU's queued arguments, rt_ops.cuh):
+// fdlibm's path for that range, 1 - 2/(expm1f(2|x|) + 2), where expm1f's
+// reduction count is k >= 2 (2|x| >= 2 > 3*ln2/2), so only its two
+// reconstructions for k in [2, 22] and [23, 56] remain (selected without
+// branches).  Its two IEEE divisions are done without the division's
+// general path: expm1f's quotient (numerator near -2, denominator in
+// [5.5, 6.5]) by fdiv_markstein, and 2/(t + 2) as 2*RN(1/(t + 2)), which is
+// the same float because 2 is a power of two (t + 2 >= 17).  Bit-identical to
+// glibc's tanhf on every float of that range (tests/native/libm_check).
+RT_HD float tanhf_glibc_ge1(float x) {
+  const float kLn2Hi = u2f(0x3f317180u), kLn2Lo = u2f(0x3717f7d1u);
+  const float kInvLn2 = u2f(0x3fb8aa3bu);
+  const float kQ1 = u2f(0xbd088889u), kQ2 = u2f(0x3ad00d01u), kQ3 = u2f(0xb8a670cdu);
+  const float kQ4 = u2f(0x36867e54u), kQ5 = u2f(0xb457edbbu);
+  const float a = fmul(2.0f, u2f(f2u(x) & 0x7fffffffu));
+  const int k = (int)fadd(fmul(kInvLn2, a), 0.5f);
+  const float tk = (float)k;
+  const float hi = fsub(a, fmul(tk, kLn2Hi));
+  const float lo = fmul(tk, kLn2Lo);
+  const float xr = fsub(hi, lo);
+  const float c = fsub(fsub(hi, xr), lo);
+  const float hfx = fmul(0.5f, xr);
+  const float hxs = fmul(xr, hfx);
+  float poly = fadd(kQ4, fmul(hxs, kQ5));
+  poly = fadd(kQ3, fmul(hxs, poly));
+  poly = fadd(kQ2, fmul(hxs, poly));
+  poly = fadd(kQ1, fmul(hxs, poly));
+  const float r1 = fadd(1.0f, fmul(hxs, poly));
+  const float t3 = fsub(3.0f, fmul(r1, hfx));
+  const float e = fmul(hxs, fdiv_markstein(fsub(r1, t3), fsub(6.0f, fmul(xr, t3))));
+  const float e2 = fsub(fsub(fmul(xr, fsub(e, c)), c), hxs);
+  const uint32_t kbits = (uint32_t)k << 23;
+  float t;
+  if (k < 23) {
+    const float one_m = u2f(0x3f800000u - (0x1000000u >> k));            // 1 - 2^-k
+    t = u2f(f2u(fsub(one_m, fsub(e2, xr))) + kbits);
+  } else {
+    const float two_mk = u2f((uint32_t)(0x7f - k) << 23);                 // 2^-k
+    t = u2f(f2u(fadd(fsub(xr, fadd(e2, two_mk)), 1.0f)) + kbits);
+  }
+  const float z = fsub(1.0f, fmul(2.0f, rcp_rn(fadd(t, 2.0f))));
   return (f2u(x) >> 31) ? -z : z;
 }
 

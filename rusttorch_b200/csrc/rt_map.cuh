@@ -163,22 +163,32 @@ map_split_kernel(const float* x, float* out, size_t n, F f) {
   const unsigned below = (1u << lane) - 1u;
   const size_t n4 = n >> 2;
   const size_t tile = (size_t)kThreads * kSplitU;
+  const size_t step = (size_t)gridDim.x * tile;
   // Every lane of a warp runs the same number of iterations (the loop bound
-  // is rounded up to whole warps), so the ballots see all 32 lanes.
+  // is the warp's first index), so the ballots see all 32 lanes.
   const size_t warp0 = (size_t)blockIdx.x * tile + (threadIdx.x & ~31u);
-  for (size_t wbase = warp0; wbase < n4; wbase += (size_t)gridDim.x * tile) {
+  auto load = [&](size_t wbase, float4* v) {
+#pragma unroll
+    for (int u = 0; u < kSplitU; u++) {
+      const size_t j = wbase + lane + (size_t)u * kThreads;
+      v[u] = j < n4 ? ld4(x + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 cur[kSplitU], nxt[kSplitU];
+  if (warp0 < n4) load(warp0, cur);
+  for (size_t wbase = warp0; wbase < n4; wbase += step) {
     const size_t base = wbase + lane;
     float xs[4 * kSplitU], t[4 * kSplitU];
     int slot[4 * kSplitU];
 #pragma unroll
     for (int u = 0; u < kSplitU; u++) {
-      const size_t j = base + (size_t)u * kThreads;
-      const float4 v = j < n4 ? ld4(x + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
-      xs[4 * u] = v.x;
-      xs[4 * u + 1] = v.y;
-      xs[4 * u + 2] = v.z;
-      xs[4 * u + 3] = v.w;
+      xs[4 * u] = cur[u].x;
+      xs[4 * u + 1] = cur[u].y;
+      xs[4 * u + 2] = cur[u].z;
+      xs[4 * u + 3] = cur[u].w;
     }
+    // the next iteration's loads are in flight during this one's arithmetic
+    if (wbase + step < n4) load(wbase + step, nxt);
     int count = 0;
 #pragma unroll
     for (int e = 0; e < 4 * kSplitU; e++) {
@@ -206,6 +216,7 @@ map_split_kernel(const float* x, float* out, size_t n, F f) {
                                      F::finish(xs[4 * u + 1], t[4 * u + 1]),
                                      F::finish(xs[4 * u + 2], t[4 * u + 2]),
                                      F::finish(xs[4 * u + 3], t[4 * u + 3])));
+      cur[u] = nxt[u];
     }
   }
   if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {

@@ -186,8 +186,8 @@ struct OpGeluTol {
     return fmul(k, fadd(x, fmul(0.044715f, x3)));
   }
   RT_HD static bool needs_exact(float z) { return z < kGeluExactBelow && z >= -9.1f; }
-  RT_HD static float fast_tanh(float z) { return z < -9.1f ? -1.0f : tanh_fast(z); }
-  RT_HD static float exact_tanh(float z) { return tanhf_glibc(z); }
+  RT_HD static float fast_tanh(float z) { return z < -9.1f ? -1.0f : tanh_fast_abs(z); }
+  RT_HD static float exact_tanh(float z) { return tanhf_glibc_ge1(z); }   // 1.4 < |z| <= 9.1
   RT_HD static float finish(float x, float t) { return fmul(fmul(0.5f, x), fadd(1.0f, t)); }
   RT_HD float operator()(float x) const {
     const float z = arg(x);

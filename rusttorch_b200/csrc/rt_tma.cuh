@@ -83,13 +83,33 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// `bytes` (a multiple of 16) from global `src` to shared `dst` (both 16-byte
+// aligned) as one bulk copy, counted on `bar` in bytes.  No multicast: the
+// copy fills the issuing CTA's shared memory only.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Host: encodes a tiled tensor map (driver entry point looked up once).
 // Returns false if the driver call is unavailable or rejects the layout.
 bool encode_tensor_map_f32(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims,
                            const uint64_t* strides_bytes, const uint32_t* box);
 
 // Host: the device-side flag a kernel sets (to 1) when it gives up a bounded
-// wait, for the current device; nullptr if it cannot be resolved.
+// wait, for the current device; nullptr if it cannot be resolved.  The
+// address is looked up once per device and kept, so the library must not be
+// used on a device after that device has been reset.
 int* wait_timeout_flag(int device);
 // Host: nonzero if a kernel on `device` gave up a bounded wait since the
 // last call (the flag is cleared).  Synchronises the device's work first.

@@ -43,12 +43,19 @@ def combine(summaries: list[ShardSummary], lib=None) -> tuple[float, float, floa
 
 class ShardedReducer:
     """sum/mean/max/min of a tensor sharded over the ranks of the default
-    process group (torch.distributed must be initialised)."""
+    process group (torch.distributed must be initialised).
 
-    def __init__(self, lib, rank: int, world: int):
+    `timeout_s` bounds the exchange: if the other ranks' summaries have not
+    all arrived after that many seconds (a rank left between steps, or never
+    reached this step), exchange() raises RusttorchError (BackendError)
+    instead of waiting for the process group's own timeout.  After that the
+    process group is not usable for further collectives: destroy it."""
+
+    def __init__(self, lib, rank: int, world: int, timeout_s: float | None = None):
         import torch
 
         self.lib, self.rank, self.world = lib, rank, world
+        self.timeout_s = timeout_s
         _bind(lib)
         dev = "cuda" if torch.cuda.is_available() else "cpu"
         self._send = torch.empty(SUMMARY_BYTES, dtype=torch.uint8, device=dev)
@@ -65,7 +72,22 @@ class ShardedReducer:
 
         ctypes.memmove(self._host.data_ptr(), ctypes.addressof(s), SUMMARY_BYTES)
         self._send.copy_(self._host, non_blocking=True)
-        dist.all_gather_into_tensor(self._recv, self._send)
+        if self.timeout_s is None:
+            dist.all_gather_into_tensor(self._recv, self._send)
+        else:
+            from datetime import timedelta
+
+            work = dist.all_gather_into_tensor(self._recv, self._send, async_op=True)
+            try:
+                done = work.wait(timeout=timedelta(seconds=self.timeout_s))
+            except Exception as e:   # the backend's timeout or a lost peer
+                raise N.RusttorchError(
+                    f"sharded stats: the shard summaries of all {self.world} ranks did not "
+                    f"arrive within {self.timeout_s} s: {e}", N.BACKEND_ERROR) from e
+            if done is False:
+                raise N.RusttorchError(
+                    f"sharded stats: the shard summaries of all {self.world} ranks did not "
+                    f"arrive within {self.timeout_s} s", N.BACKEND_ERROR)
         raw = self._recv.cpu().numpy().tobytes()
         return [ShardSummary.from_buffer_copy(raw, i * SUMMARY_BYTES) for i in range(self.world)]
 

@@ -6,11 +6,15 @@ a GPU.  The expected texts are rusttorch's TensorError Display strings
 Descriptors point at a dummy address: nothing is dereferenced on these paths.
 """
 import ctypes
+import os
 import subprocess
+from pathlib import Path
 
 import pytest
 
 from rusttorch_b200 import _native as N
+
+ROOT = Path(__file__).resolve().parents[1]
 
 DUMMY = 0x1000
 
@@ -216,3 +220,29 @@ def test_tensor_desc_keeps_its_tensor_alive():
     assert (s.ndim, s.numel, s.shape[0], s.shape[1], s.data) == (2, 6, 2, 3, 0x1000)
     del ref, s
     assert alive() is None                  # no cycle: freed without the collector
+
+
+def test_nvtx_ranges_switched_on_by_the_environment():
+    """RTC_NVTX=1 wraps every op in an NVTX range named after its entry point
+    (read once per process, so this runs in a fresh one); calls behave the
+    same with it on: a call that fails validation (no GPU needed) returns the
+    same code and message as without it."""
+    import sys
+    code = (
+        "from rusttorch_b200 import _native as N\n"
+        "a = N.Desc(0, [2, 3], N.F32, 0)\n"
+        "b = N.Desc(0, [3, 2], N.I32, 0)\n"
+        "r = N.lib().rtc_add(a.ref, b.ref, a.ref)\n"
+        "import ctypes\n"
+        "print(r.code, ctypes.string_at(r.error_msg).decode())\n")
+    env = dict(os.environ, RTC_NVTX="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, cwd=str(ROOT),
+                         capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    a = N.Desc(0, [2, 3], N.F32, 0)
+    b = N.Desc(0, [3, 2], N.I32, 0)
+    r = N.lib().rtc_add(a.ref, b.ref, a.ref)
+    want = f"{r.code} {ctypes.string_at(r.error_msg).decode()}"
+    N.lib().rtc_free_error_message(r.error_msg)
+    assert not r.success
+    assert out.stdout.strip() == want

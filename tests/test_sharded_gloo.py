@@ -120,3 +120,55 @@ def test_two_gloo_ranks_match_the_whole_tensor():
 def test_combine_of_empty_is_an_error():
     with pytest.raises(ValueError, match="empty tensor"):
         sharded.combine([sharded.ShardSummary()])
+
+
+# ------------------------------------------------- a rank that leaves
+# Failure detection on the host (no GPU is involved): two gloo ranks run the
+# sharded reduction's exchange for one step; then rank 1 either stays alive
+# without joining the next step or exits.  Rank 0's ShardedReducer, built
+# with a short timeout, must raise instead of waiting for the process
+# group's own timeout (set long here, 120 s, so it cannot be what ends it).
+LIMIT_S = 3.0
+
+
+def _leaving_worker(rank, world, port, mode, q):
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    red = sharded.ShardedReducer(sharded.N.lib(), rank, world, timeout_s=LIMIT_S)
+    s = summary_of(O.normal(1000, 7 + rank))
+    first = red.exchange(s)                       # step 1: everyone takes part
+    if rank == 1:
+        if mode == "stays":
+            time.sleep(LIMIT_S + 4)               # alive, never joins step 2
+        os._exit(0)                               # or simply gone
+    t0 = time.perf_counter()
+    try:
+        red.exchange(s)
+        q.put(("no error", time.perf_counter() - t0, len(first)))
+    except ValueError as e:
+        q.put((getattr(e, "kind", type(e).__name__), time.perf_counter() - t0, str(e)[:200]))
+    q.close()
+    q.join_thread()                               # deliver the result before leaving
+    os._exit(0)                                   # the group is broken: no teardown
+
+
+@pytest.mark.parametrize("mode", ["stays", "exits"])
+def test_survivor_reports_a_rank_that_left_within_the_limit(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, mode, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    kind, elapsed, detail = q.get(timeout=90)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert kind == "BackendError", (kind, detail)
+    assert elapsed < LIMIT_S + 5.0, (elapsed, detail)
