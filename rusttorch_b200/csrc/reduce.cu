@@ -734,50 +734,83 @@ lane_sum8_quad_kernel(const float* x, size_t lanes, size_t len, float* out, int 
 }
 
 // ------------------------------------------ last-axis sum, chains read directly
-// The same eight chains per row as above, four rows per warp, each thread
-// running one chain (thread 8r + j: chain j of the warp's row r), but every
-// chain reads its own floats straight from global memory with 4-byte loads
-// (x[8k + j] for k = 0, 1, ...): the eight threads of a row read 32
-// consecutive bytes, one full sector, so no byte is fetched twice and nothing
-// passes through shared memory.  K loads per thread are in flight while the
-// previous K are added (double-buffered registers), ~2 instructions per
-// element instead of the staged kernel's ~13; any alignment, any len >= 8.
-template <int WARPS, int K>
+// The same eight chains per row as above, each run by one thread, but every
+// chain reads its own floats straight from global memory: with CPT chains
+// per thread (1, 2 or 4 adjacent chains, read together as a float, float2 or
+// float4 at x[8k + CPT*j]), 8/CPT threads cover a row and read 32
+// consecutive bytes of it per step, so no byte is fetched twice and nothing
+// passes through shared memory; a warp holds 32*CPT/8 rows.  K loads per
+// thread are in flight while the previous K are added (double-buffered
+// registers), ~2 instructions per element instead of the staged kernel's
+// ~13.  CPT > 1 needs rows aligned to 4*CPT bytes.
+template <int CPT>
+struct ChainVec;
+template <>
+struct ChainVec<1> {
+  using T = float;
+  __device__ static float get(const T& v, int) { return v; }
+};
+template <>
+struct ChainVec<2> {
+  using T = float2;
+  __device__ static float get(const T& v, int c) { return c ? v.y : v.x; }
+};
+template <>
+struct ChainVec<4> {
+  using T = float4;
+  __device__ static float get(const T& v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+  }
+};
+
+template <int WARPS, int K, int CPT>
 __global__ void __launch_bounds__(WARPS * 32)
 lane_sum8_direct_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  using V = typename ChainVec<CPT>::T;
+  constexpr int TPR = 8 / CPT, RPW = 32 / TPR;      // threads per row, rows per warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t r0 = ((size_t)blockIdx.x * WARPS + warp) * 4;
+  const size_t r0 = ((size_t)blockIdx.x * WARPS + warp) * RPW;
   if (r0 >= lanes) return;                             // whole warp leaves together
-  const int rr = lane >> 3, j = lane & 7;
+  const int rr = lane / TPR, j = lane % TPR;
   const size_t row = r0 + rr;
   const bool live = row < lanes;
   const float* xr = x + (live ? row : r0) * len;       // idle lanes reread row r0
-  const float* p = xr + j;
+  const V* p = reinterpret_cast<const V*>(xr + CPT * j);
+  constexpr int kStep = 8 / CPT;                       // V elements per chain step
   const size_t steps = len / 8;                        // chain steps per row
-  float acc = 0.0f;
+  float acc[CPT];
+#pragma unroll
+  for (int c = 0; c < CPT; c++) acc[c] = 0.0f;
+  auto add = [&](const V& v) {
+#pragma unroll
+    for (int c = 0; c < CPT; c++) acc[c] = fadd(acc[c], ChainVec<CPT>::get(v, c));
+  };
   size_t k = 0;
   if (steps >= (size_t)K) {
-    float cur[K];
+    V cur[K];
 #pragma unroll
-    for (int u = 0; u < K; u++) cur[u] = __ldcs(p + 8 * u);
-    p += 8 * K;
+    for (int u = 0; u < K; u++) cur[u] = __ldcs(p + kStep * u);
+    p += kStep * K;
     for (k = K; k + K <= steps; k += K) {
-      float nxt[K];
+      V nxt[K];
 #pragma unroll
-      for (int u = 0; u < K; u++) nxt[u] = __ldcs(p + 8 * u);
-      p += 8 * K;
+      for (int u = 0; u < K; u++) nxt[u] = __ldcs(p + kStep * u);
+      p += kStep * K;
 #pragma unroll
-      for (int u = 0; u < K; u++) acc = fadd(acc, cur[u]);
+      for (int u = 0; u < K; u++) add(cur[u]);
 #pragma unroll
       for (int u = 0; u < K; u++) cur[u] = nxt[u];
     }
 #pragma unroll
-    for (int u = 0; u < K; u++) acc = fadd(acc, cur[u]);
+    for (int u = 0; u < K; u++) add(cur[u]);
   }
-  for (; k < steps; k++, p += 8) acc = fadd(acc, __ldcs(p));
+  for (; k < steps; k++, p += kStep) add(__ldcs(p));
   float q[8];
 #pragma unroll
-  for (int t = 0; t < 8; t++) q[t] = __shfl_sync(0xffffffffu, acc, (lane & ~7) + t);
+  for (int t = 0; t < TPR; t++)
+#pragma unroll
+    for (int c = 0; c < CPT; c++)
+      q[t * CPT + c] = __shfl_sync(0xffffffffu, acc[c], (lane & ~(TPR - 1)) + t);
   if (j == 0 && live) {
     float r = 0.0f;
     r = fadd(r, fadd(q[0], q[4]));
@@ -790,14 +823,14 @@ lane_sum8_direct_kernel(const float* x, size_t lanes, size_t len, float* out, in
   }
 }
 
-template <int WARPS, int K>
+template <int WARPS, int K, int CPT = 1>
 void launch_lane_direct_w(const float* x, size_t lanes, size_t len, float* out, bool mean,
                           cudaStream_t s) {
-  const size_t per_cta = (size_t)WARPS * 4;      // rows
+  const size_t per_cta = (size_t)WARPS * (32 * CPT / 8);      // rows
   const size_t grid = (lanes + per_cta - 1) / per_cta;
   for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
     const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
-    lane_sum8_direct_kernel<WARPS, K><<<(unsigned)ng, WARPS * 32, 0, s>>>(
+    lane_sum8_direct_kernel<WARPS, K, CPT><<<(unsigned)ng, WARPS * 32, 0, s>>>(
         x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta, mean);
   }
 }
@@ -935,20 +968,21 @@ cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts,
 
 cudaError_t launch_lane_sum_variant(int warps, const float* x, size_t lanes, size_t len,
                                     float* out, cudaStream_t s) {
-  if (warps == 99) {   // the bulk-copy ring kernel
-    bool used = false;
-    const cudaError_t e = launch_lane_sum_bulk(x, lanes, len, out, false, s, &used);
-    return used ? e : cudaErrorInvalidValue;
-  }
-  // warps < 0: the direct kernel with -warps = 10*K + warps per CTA (K = 16, 32)
+  // warps < 0: the direct kernel with -warps = 1000*CPT + 10*K + warps per CTA
   if (warps < 0) {
-    const int code = -warps, K = code / 10, w = code % 10;
-    if (len < 8) return cudaErrorInvalidValue;
-    if (K == 16 && w == 2) launch_lane_direct_w<2, 16>(x, lanes, len, out, false, s);
-    else if (K == 32 && w == 1) launch_lane_direct_w<1, 32>(x, lanes, len, out, false, s);
-    else if (K == 32 && w == 2) launch_lane_direct_w<2, 32>(x, lanes, len, out, false, s);
-    else if (K == 32 && w == 4) launch_lane_direct_w<4, 32>(x, lanes, len, out, false, s);
-    else if (K == 64 && w == 2) launch_lane_direct_w<2, 64>(x, lanes, len, out, false, s);
+    const int code = -warps, cpt = code / 1000, K = (code / 10) % 100, w = code % 10;
+    if (len < 8 || (cpt > 1 && ((reinterpret_cast<uintptr_t>(x) | len * 4) % (4 * cpt)) != 0))
+      return cudaErrorInvalidValue;
+    if (cpt == 1 && K == 32 && w == 2) launch_lane_direct_w<2, 32, 1>(x, lanes, len, out, false, s);
+    else if (cpt == 2 && K == 16 && w == 2) launch_lane_direct_w<2, 16, 2>(x, lanes, len, out, false, s);
+    else if (cpt == 2 && K == 32 && w == 2) launch_lane_direct_w<2, 32, 2>(x, lanes, len, out, false, s);
+    else if (cpt == 2 && K == 24 && w == 2) launch_lane_direct_w<2, 24, 2>(x, lanes, len, out, false, s);
+    else if (cpt == 2 && K == 32 && w == 1) launch_lane_direct_w<1, 32, 2>(x, lanes, len, out, false, s);
+    else if (cpt == 2 && K == 32 && w == 4) launch_lane_direct_w<4, 32, 2>(x, lanes, len, out, false, s);
+    else if (cpt == 1 && K == 48 && w == 2) launch_lane_direct_w<2, 48, 1>(x, lanes, len, out, false, s);
+    else if (cpt == 4 && K == 8 && w == 2) launch_lane_direct_w<2, 8, 4>(x, lanes, len, out, false, s);
+    else if (cpt == 4 && K == 16 && w == 1) launch_lane_direct_w<1, 16, 4>(x, lanes, len, out, false, s);
+    else if (cpt == 4 && K == 16 && w == 2) launch_lane_direct_w<2, 16, 4>(x, lanes, len, out, false, s);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
   }
@@ -1036,14 +1070,16 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     } else if (len >= 1024 && lanes >= (size_t)sm_count(cur_device()) * 28) {
       // enough lanes for ~7 warps per SM (fewer leave the warp kernel
       // under-occupied; the staged kernel below spreads 4 lanes per CTA):
-      // rows through a cp.async.bulk ring when they are 16-byte aligned
-      // (lane_bulk.cu), else the chains read straight from global memory
-      // (0.795 of the measured bandwidth at cfg3 against 0.737 for the
-      // shared-memory-staged lane_sum8_quad_kernel, bench.py --probe)
-      bool used = false;
-      const cudaError_t e = launch_lane_sum_bulk(x, lanes, len, out, op == kDimMean, s, &used);
-      if (e != cudaSuccess) return e;
-      if (!used) launch_lane_direct_w<2, 32>(x, lanes, len, out, op == kDimMean, s);
+      // the chains read straight from global memory, two adjacent chains
+      // per thread (float2 loads) when the rows are 8-byte aligned: 0.83 of
+      // the measured bandwidth at cfg3, against 0.80-0.81 with one chain per
+      // thread, 0.59 with four, 0.74-0.75 for the shared-memory-staged
+      // lane_sum8_quad_kernel and 0.665 for rows streamed through a
+      // cp.async.bulk ring (bench.py --probe)
+      if ((reinterpret_cast<uintptr_t>(x) & 7u) == 0 && len % 2 == 0)
+        launch_lane_direct_w<2, 32, 2>(x, lanes, len, out, op == kDimMean, s);
+      else
+        launch_lane_direct_w<2, 32, 1>(x, lanes, len, out, op == kDimMean, s);
     } else if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 4 == 0 && len >= 64) {
       const size_t grid = (lanes + kLsRows - 1) / kLsRows;
       // deepest ring whose CTAs are all resident in one wave (else 4)

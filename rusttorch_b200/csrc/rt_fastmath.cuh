@@ -53,7 +53,8 @@ struct ExpParts {
   float p, s1, s2;
 };
 
-RT_HD ExpParts exp_parts(float x) {
+// e^x = p * 2^k (p in [0.70, 1.42]) for x in [-104, 89] (or NaN).
+RT_HD float exp_core(float x, int* kout) {
   const float kLog2e = u2f(0x3fb8aa3bu);
   const float kShift = 12582912.0f;           // 1.5 * 2^23
   const float kLn2Hi = u2f(0x3f317218u);      // ln2 rounded to float
@@ -71,7 +72,13 @@ RT_HD ExpParts exp_parts(float x) {
   h = ffma(h, r, kE1);
   h = ffma(h, r, kE0);
   h = ffma(h, r, 1.0f);                       // 1 + r*E(r)
-  const float p = ffma(h, r, 1.0f);           // 1 + r + r^2*E(r)
+  *kout = k;
+  return ffma(h, r, 1.0f);                    // 1 + r + r^2*E(r)
+}
+
+RT_HD ExpParts exp_parts(float x) {
+  int k;
+  const float p = exp_core(x, &k);
   const int k1 = k >> 1, k2 = k - k1;
   return ExpParts{p, u2f((uint32_t)(k1 + 127) << 23), u2f((uint32_t)(k2 + 127) << 23)};
 }
@@ -117,13 +124,16 @@ RT_HD float tanh_fast(float x) {
 // relative accuracy of tanh itself, not absolute.
 RT_HD float tanh_fast_abs(float z) {
   const float az = fabs_bits(z);
-  const ExpParts e = exp_parts(fmul(2.0f, az > 9.5f ? 9.5f : az));
-  const float t = ffma(-2.0f, rcp_cr(fadd(fmul(fmul(e.p, e.s1), e.s2), 1.0f)), 1.0f);
+  // 2|z| <= 19, so 2^k with k <= 28 is one normal power of two: e = p * 2^k.
+  int k;
+  const float p = exp_core(fmul(2.0f, az > 9.5f ? 9.5f : az), &k);
+  const float t = ffma(-2.0f, rcp_cr(fadd(fmul(p, u2f((uint32_t)(k + 127) << 23)), 1.0f)), 1.0f);
   return u2f(f2u(t) | (f2u(z) & 0x80000000u));
 }
 
-// log(y) for a positive normal finite y (or NaN).
-RT_HD float log_fast(float y) {
+// log(y) for a positive normal finite y (garbage, but no fault, for other
+// inputs, NaN included: callers that can see a NaN use log_fast).
+RT_HD float log_fast_pos(float y) {
   const float kLn2Hi = u2f(0x3f317218u), kLn2Lo = u2f(0xb102e308u);
   // L(f) = (log1p(f) - f + f^2/2)/f^3, highest degree first
   const float kL7 = u2f(0xbda1d923u), kL6 = u2f(0x3e0140a7u), kL5 = u2f(0xbe0519f5u);
@@ -142,7 +152,12 @@ RT_HD float log_fast(float y) {
   h = ffma(h, f, kL0);
   const float l = ffma(fmul(f, f), ffma(h, f, -0.5f), f);
   const float kf = (float)k;
-  const float r = ffma(kf, kLn2Hi, ffma(kf, kLn2Lo, l));
+  return ffma(kf, kLn2Hi, ffma(kf, kLn2Lo, l));
+}
+
+// log(y) for a positive normal finite y, or NaN for NaN.
+RT_HD float log_fast(float y) {
+  const float r = log_fast_pos(y);
   return y != y ? y : r;
 }
 

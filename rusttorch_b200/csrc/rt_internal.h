@@ -110,12 +110,6 @@ cudaError_t launch_stats_gs_variant(int threads, int u, int blocks_per_sm, const
                                     size_t n, StatsPart* parts, int max_parts, cudaStream_t s,
                                     double* sum_out);
 
-// The last-axis sum (mean) of [lanes, len] through a cp.async.bulk ring
-// (lane_bulk.cu); *used = false (nothing launched) when the layout does not
-// suit it (unaligned rows, len < 1024).
-cudaError_t launch_lane_sum_bulk(const float* x, size_t lanes, size_t len, float* out, bool mean,
-                                 cudaStream_t s, bool* used);
-
 // The last-axis sum of [lanes, len] (len % 4 == 0, 16-byte-aligned x) by
 // the four-lanes-per-warp kernel with `warps` (1, 2, 4, 8) warps per CTA.
 // For the probes.

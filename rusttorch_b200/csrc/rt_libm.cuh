@@ -251,6 +251,12 @@ RT_HD float expf_glibc(float x) {
   return expf_glibc_core(lo > 89.0f ? 89.0f : lo);
 }
 
+// expf_glibc for x <= 89 (or NaN), clamped below only: softplus and mish
+// use exp(x) only for x <= 20 and ignore whatever the core returns above 89.
+RT_HD float expf_glibc_le89(float x) {
+  return expf_glibc_core(x < -104.0f ? -104.0f : x);
+}
+
 // expf for x <= 0 or NaN (softmax's x - max), without expf_glibc's range
 // branches: x below -104 (including -inf) is replaced by -104, whose exp the
 // core path rounds to +0 exactly as glibc's underflow branch returns for

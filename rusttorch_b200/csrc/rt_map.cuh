@@ -9,6 +9,7 @@
 // kernel gives the same results.
 #pragma once
 #include "rt_internal.h"
+#include "rt_libm.cuh"
 
 #include <algorithm>
 #include <type_traits>

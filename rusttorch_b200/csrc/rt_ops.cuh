@@ -150,7 +150,9 @@ struct OpTanhTol {
 // decides the result's leading digits, and only the log is approximated.
 struct OpSoftplusTol {
   RT_HD float operator()(float x) const {
-    return x > 20.0f ? x : log_fast(fadd(1.0f, expf_glibc(x)));
+    // !(x <= 20): x > 20, or x NaN (returned as is); below, 1 + exp(x) is a
+    // positive normal float in [1, 4.9e8]
+    return !(x <= 20.0f) ? x : log_fast_pos(fadd(1.0f, expf_glibc_le89(x)));
   }
 };
 // :284 mish = x * tanh(softplus(x)).  With y = 1 + exp(x) (the reference's
@@ -159,7 +161,7 @@ struct OpSoftplusTol {
 // x > 20 the reference's tanh(x) is 1, so mish is x.
 struct OpMishTol {
   RT_HD float operator()(float x) const {
-    const float y = fadd(1.0f, expf_glibc(x));
+    const float y = fadd(1.0f, expf_glibc_le89(x));   // exp(x) is used only for x <= 20
     const float num = fmul(fsub(y, 1.0f), fadd(y, 1.0f));
     const float t = fmul(num, rcp_cr(ffma(y, y, 1.0f)));
     return x > 20.0f ? x : fmul(x, t);
@@ -186,7 +188,8 @@ struct OpGeluTol {
     return fmul(k, fadd(x, fmul(0.044715f, x3)));
   }
   RT_HD static bool needs_exact(float z) { return z < kGeluExactBelow && z >= -9.1f; }
-  RT_HD static float fast_tanh(float z) { return z < -9.1f ? -1.0f : tanh_fast_abs(z); }
+  // -1 exactly below -8.9 (2/(e^(2|z|) + 1) < 2^-25 there), as glibc's tanhf
+  RT_HD static float fast_tanh(float z) { return tanh_fast_abs(z); }
   RT_HD static float exact_tanh(float z) { return tanhf_glibc_ge1(z); }   // 1.4 < |z| <= 9.1
   RT_HD static float finish(float x, float t) { return fmul(fmul(0.5f, x), fadd(1.0f, t)); }
   RT_HD float operator()(float x) const {

@@ -88,7 +88,8 @@ def test_sharded_errors_launch_nothing():
     P = shards_of(x, [500])
     G = shards_of(x, [500])
     M = shards_of(x, [500])
-    V = [rt.Tensor.from_numpy(np.zeros(500, np.float32)), rt.Tensor.from_numpy(np.zeros(7, np.float32))]
+    V = [rt.Tensor.from_numpy(np.zeros(500, np.float32), device=0),
+         rt.Tensor.from_numpy(np.zeros(7, np.float32), device=1 % ngpu())]
     with pytest.raises(N.RusttorchError) as e:
         rt.sharded_adamw_update(P, G, M, V, 1e-3, 0.9, 0.999, 1e-8, 0.01, 10)
     assert e.value.code == N.SHAPE_MISMATCH
