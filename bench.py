@@ -805,6 +805,16 @@ def run_probe(args) -> None:
     dst = torch.empty_like(src)
     only = re.compile(args.only) if args.only else None
 
+    def lanes_match(p0, nb):
+        """The lane-sum probe's output (dst) against the library's sum_dim(1)
+        of the same [nb/4/p0, p0] view, bit for bit."""
+        lanes = (nb // 4) // p0
+        xs = N.Desc(src.data_ptr(), [lanes, p0], N.F32, 0)
+        ref = torch.empty(lanes, dtype=torch.float32, device="cuda")
+        N.check(lib.rtc_sum_dim(xs.ref, 1, N.Desc(ref.data_ptr(), [lanes], N.F32, 0).ref))
+        torch.cuda.synchronize()
+        return bool(torch.equal(ref.view(torch.int32), dst[:lanes].view(torch.int32)))
+
     def timeit(name, mode, nb, algo_bytes, p0, p1, p2, dirty=False):
         """dirty=False: L2 flushed by writing 256 MiB and then reading another
         256 MiB, so the timed kernel starts on clean lines; dirty=True: the
@@ -830,10 +840,12 @@ def run_probe(args) -> None:
         N.check(lib.rtc_synchronize())
         ms = statistics.median(times)
         gbs = algo_bytes / (ms * 1e-3) / 1e9
-        print(json.dumps({"probe": name, "mode": mode, "p": [p0, p1, p2], "ms": ms, "GB_s": gbs,
-                          "frac_of_measured_peak": gbs / peak, "bytes": algo_bytes,
-                          "l2": "dirty" if dirty else "clean", "repeat": args.repeat}),
-              flush=True)
+        line = {"probe": name, "mode": mode, "p": [p0, p1, p2], "ms": ms, "GB_s": gbs,
+                "frac_of_measured_peak": gbs / peak, "bytes": algo_bytes,
+                "l2": "dirty" if dirty else "clean", "repeat": args.repeat}
+        if mode == 8:
+            line["matches_sum_dim"] = lanes_match(p0, nb)
+        print(json.dumps(line), flush=True)
 
     # u < 0: the stats kernel with float32 trees per float4 (|u| loads in flight)
     for threads, u, bps in ((256, 8, 0), (512, 4, 0), (512, 8, 0), (256, -4, 0), (256, -8, 0),
@@ -843,8 +855,9 @@ def run_probe(args) -> None:
                             (512, 2, 104), (256, 4, 108)):
         timeit(f"stats kernel t{threads} u{u} b{bps}", 7, nbytes, nbytes, threads, u, bps)
     # cfg3's sum_dim(1): [8192, 16384]; negative: the direct-chain kernel,
-    # -(1000*CPT + 10*K + warps per CTA), CPT chains per thread
-    for warps in (2, -1322, -1482, -2322, -2242, -2321, -2324):
+    # -(1000*CPT + 10*K + warps per CTA), CPT chains per thread; >= 100: the
+    # 128-byte-read transpose kernel, 100*K + warps per CTA
+    for warps in (-1322, -2322, 802, 1602, 1601, 1604):
         timeit(f"lane sum [8192,16384] warps/CTA {warps}", 8, 4 * R3 * C3, 4 * R3 * C3 + 4 * R3,
                C3, warps, 0)
     for dirty in (False, True):

@@ -471,7 +471,8 @@ rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output, const rtc_t
  * and p2 blocks per SM (0: all that stay resident); 8: the last-axis sum of
  * src viewed as [bytes/4/p0, p0] into dst: p1 (1, 2, 4, 8) warps per CTA of the
  * shared-memory-staged kernel, -(1000*C + 10*K + w) the direct-chain kernel
- * (C chains per thread, K loads ahead, w warps per CTA).
+ * (C chains per thread, K loads ahead, w warps per CTA), 100*K + w (>= 100)
+ * the 128-byte-read transpose kernel.
  * Device pointers on the current GPU, 16-byte aligned; returns once queued. */
 rtc_result rtc_probe_stream(int mode, const void* src, void* dst, size_t bytes, int p0, int p1,
                             int p2);

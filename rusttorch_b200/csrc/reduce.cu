@@ -823,6 +823,98 @@ lane_sum8_direct_kernel(const float* x, size_t lanes, size_t len, float* out, in
   }
 }
 
+// ---------------------------- last-axis sum, 128-byte row reads + transpose
+// Four rows per warp, one thread per ndarray chain, as lane_sum8_direct, but
+// the eight threads of a row read 128 contiguous bytes per load instruction
+// (a float4 each: 32 floats = four chain steps of all eight chains) instead
+// of 32.  Thread (q, g) of a row (sub-lane 2q + g) loads floats 4(2q+g) ..+3,
+// i.e. step 4s + q of chains 4g..4g+3; a 4x4 transpose among the four
+// threads of each g (two butterfly levels of two shuffles each) leaves
+// thread (q, g) holding steps 4s..4s+3 of chain 4g + q, which it adds in
+// order.  Needs len % 32 == 0 and 16-byte-aligned rows.
+__device__ __forceinline__ void transpose4(float v[4], unsigned q) {
+#pragma unroll
+  for (int b = 1; b <= 2; b <<= 1) {
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      if (c & b) continue;
+      const bool hi = (q & (unsigned)b) != 0;
+      const float send = hi ? v[c] : v[c ^ b];
+      const float got = __shfl_xor_sync(0xffffffffu, send, 2 * b);
+      if (hi) v[c] = got;
+      else v[c ^ b] = got;
+    }
+  }
+}
+
+template <int WARPS, int K>
+__global__ void __launch_bounds__(WARPS * 32)
+lane_sum8_tr_kernel(const float* x, size_t lanes, size_t len, float* out, int mean) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t r0 = ((size_t)blockIdx.x * WARPS + warp) * 4;
+  if (r0 >= lanes) return;                             // whole warp leaves together
+  const int rr = lane >> 3, sub = lane & 7;
+  const unsigned q = (unsigned)sub >> 1, g = (unsigned)sub & 1u;
+  const size_t row = r0 + rr;
+  const bool live = row < lanes;
+  const float4* p = reinterpret_cast<const float4*>(x + (live ? row : r0) * len) + sub;
+  const size_t segs = len / 32;                        // 32-float segments per row
+  float acc = 0.0f;
+  auto add = [&](float4 f) {
+    float v[4] = {f.x, f.y, f.z, f.w};
+    transpose4(v, q);
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc = fadd(acc, v[c]);
+  };
+  size_t k = 0;
+  if (segs >= (size_t)K) {
+    float4 cur[K];
+#pragma unroll
+    for (int u = 0; u < K; u++) cur[u] = __ldcs(p + 8 * u);
+    p += 8 * K;
+    for (k = K; k + K <= segs; k += K) {
+      float4 nxt[K];
+#pragma unroll
+      for (int u = 0; u < K; u++) nxt[u] = __ldcs(p + 8 * u);
+      p += 8 * K;
+#pragma unroll
+      for (int u = 0; u < K; u++) add(cur[u]);
+#pragma unroll
+      for (int u = 0; u < K; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < K; u++) add(cur[u]);
+  }
+  for (; k < segs; k++, p += 8) add(__ldcs(p));
+  // thread (q, g) holds chain 4g + q; gather the row's eight chains
+  const int base = lane & ~7;
+  float pch[8];
+#pragma unroll
+  for (int c = 0; c < 8; c++) pch[c] = __shfl_sync(0xffffffffu, acc, base + 2 * (c & 3) + (c >> 2));
+  if (sub == 0 && live) {
+    float r = 0.0f;
+    r = fadd(r, fadd(pch[0], pch[4]));
+    r = fadd(r, fadd(pch[1], pch[5]));
+    r = fadd(r, fadd(pch[2], pch[6]));
+    r = fadd(r, fadd(pch[3], pch[7]));
+    if (mean) r = fdiv(r, (float)len);
+    out[row] = r;
+  }
+  (void)g;
+}
+
+template <int WARPS, int K>
+void launch_lane_tr_w(const float* x, size_t lanes, size_t len, float* out, bool mean,
+                      cudaStream_t s) {
+  const size_t per_cta = (size_t)WARPS * 4;
+  const size_t grid = (lanes + per_cta - 1) / per_cta;
+  for (size_t g0 = 0; g0 < grid; g0 += 0x7fffffffull) {
+    const size_t ng = std::min<size_t>(grid - g0, 0x7fffffffull);
+    lane_sum8_tr_kernel<WARPS, K><<<(unsigned)ng, WARPS * 32, 0, s>>>(
+        x + g0 * per_cta * len, lanes - g0 * per_cta, len, out + g0 * per_cta, mean);
+  }
+}
+
 template <int WARPS, int K, int CPT = 1>
 void launch_lane_direct_w(const float* x, size_t lanes, size_t len, float* out, bool mean,
                           cudaStream_t s) {
@@ -968,6 +1060,17 @@ cudaError_t launch_stats(const float* x, size_t n, StatsPart* parts, int nparts,
 
 cudaError_t launch_lane_sum_variant(int warps, const float* x, size_t lanes, size_t len,
                                     float* out, cudaStream_t s) {
+  // warps >= 100: the 128-byte-read transpose kernel, warps = 100*K + warps per CTA
+  if (warps >= 100) {
+    const int K = warps / 100, w = warps % 100;
+    if (len % 32 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return cudaErrorInvalidValue;
+    if (K == 8 && w == 2) launch_lane_tr_w<2, 8>(x, lanes, len, out, false, s);
+    else if (K == 16 && w == 2) launch_lane_tr_w<2, 16>(x, lanes, len, out, false, s);
+    else if (K == 16 && w == 1) launch_lane_tr_w<1, 16>(x, lanes, len, out, false, s);
+    else if (K == 16 && w == 4) launch_lane_tr_w<4, 16>(x, lanes, len, out, false, s);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+  }
   // warps < 0: the direct kernel with -warps = 1000*CPT + 10*K + warps per CTA
   if (warps < 0) {
     const int code = -warps, cpt = code / 1000, K = (code / 10) % 100, w = code % 10;
