@@ -857,7 +857,7 @@ def run_probe(args) -> None:
     # cfg3's sum_dim(1): [8192, 16384]; negative: the direct-chain kernel,
     # -(1000*CPT + 10*K + warps per CTA), CPT chains per thread; >= 100: the
     # 128-byte-read transpose kernel, 100*K + warps per CTA
-    for warps in (-1322, -2322, 802, 1602, 1601, 1604):
+    for warps in (-2322, 802, 804, 808, 1202, 1204, 1602, 1604, 1608):
         timeit(f"lane sum [8192,16384] warps/CTA {warps}", 8, 4 * R3 * C3, 4 * R3 * C3 + 4 * R3,
                C3, warps, 0)
     for dirty in (False, True):

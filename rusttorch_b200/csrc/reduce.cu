@@ -1065,9 +1065,14 @@ cudaError_t launch_lane_sum_variant(int warps, const float* x, size_t lanes, siz
     const int K = warps / 100, w = warps % 100;
     if (len % 32 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return cudaErrorInvalidValue;
     if (K == 8 && w == 2) launch_lane_tr_w<2, 8>(x, lanes, len, out, false, s);
+    else if (K == 8 && w == 4) launch_lane_tr_w<4, 8>(x, lanes, len, out, false, s);
+    else if (K == 8 && w == 8) launch_lane_tr_w<8, 8>(x, lanes, len, out, false, s);
+    else if (K == 12 && w == 2) launch_lane_tr_w<2, 12>(x, lanes, len, out, false, s);
+    else if (K == 12 && w == 4) launch_lane_tr_w<4, 12>(x, lanes, len, out, false, s);
     else if (K == 16 && w == 2) launch_lane_tr_w<2, 16>(x, lanes, len, out, false, s);
     else if (K == 16 && w == 1) launch_lane_tr_w<1, 16>(x, lanes, len, out, false, s);
     else if (K == 16 && w == 4) launch_lane_tr_w<4, 16>(x, lanes, len, out, false, s);
+    else if (K == 16 && w == 8) launch_lane_tr_w<8, 16>(x, lanes, len, out, false, s);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
   }
@@ -1173,13 +1178,18 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
     } else if (len >= 1024 && lanes >= (size_t)sm_count(cur_device()) * 28) {
       // enough lanes for ~7 warps per SM (fewer leave the warp kernel
       // under-occupied; the staged kernel below spreads 4 lanes per CTA):
-      // the chains read straight from global memory, two adjacent chains
-      // per thread (float2 loads) when the rows are 8-byte aligned: 0.83 of
-      // the measured bandwidth at cfg3, against 0.80-0.81 with one chain per
-      // thread, 0.59 with four, 0.74-0.75 for the shared-memory-staged
-      // lane_sum8_quad_kernel and 0.665 for rows streamed through a
-      // cp.async.bulk ring (bench.py --probe)
-      if ((reinterpret_cast<uintptr_t>(x) & 7u) == 0 && len % 2 == 0)
+      // the chains read straight from global memory.  Rows of whole
+      // 128-byte segments on 16-byte boundaries: eight threads per row,
+      // 16-byte loads and a 4x4 shuffle transpose, 16 loads in flight per
+      // thread, 8 warps per CTA (0.85-0.86 of the measured bandwidth at
+      // cfg3 for one launch, 0.89 for launches back to back).  Else two
+      // adjacent chains per thread (float2 loads) when the rows are 8-byte
+      // aligned (0.81-0.83), else one (0.80).  Four chains per thread reach
+      // 0.59, the shared-memory-staged lane_sum8_quad_kernel 0.74-0.75 and
+      // rows streamed through a cp.async.bulk ring 0.665 (bench.py --probe)
+      if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len % 32 == 0)
+        launch_lane_tr_w<8, 16>(x, lanes, len, out, op == kDimMean, s);
+      else if ((reinterpret_cast<uintptr_t>(x) & 7u) == 0 && len % 2 == 0)
         launch_lane_direct_w<2, 32, 2>(x, lanes, len, out, op == kDimMean, s);
       else
         launch_lane_direct_w<2, 32, 1>(x, lanes, len, out, op == kDimMean, s);

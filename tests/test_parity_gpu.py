@@ -356,11 +356,13 @@ def test_tma_strip_shapes(shape, dim, op):
 
 
 @pytest.mark.parametrize("shape", [(13, 1028), (1, 1024), (1000, 2052), (7, 8196), (4099, 4096),
-                                   (3, 5, 1100), (5001, 1028), (4200, 2052), (9000, 1024)])
+                                   (3, 5, 1100), (5001, 1028), (4200, 2052), (9000, 1024),
+                                   (4147, 1056), (6001, 4128)])
 @pytest.mark.parametrize("op", ["sum", "mean"])
 def test_last_axis_sum_row_kernels(shape, op):
     """Last-axis sums of rows of >= 1024 floats (four rows per warp once there
-    are enough lanes, the staged kernel below that): ragged last tiles, a tail
+    are enough lanes, read as 128-byte segments when a row is whole segments,
+    the staged kernel below that): ragged last tiles, a tail
     of len % 8 elements, lanes not a multiple of four or of the 32 rows per
     block, NaN and -0.0 in the data."""
     x = O.normal(int(np.prod(shape)), 62, 0, 2).reshape(shape)
