@@ -815,6 +815,16 @@ def run_probe(args) -> None:
         torch.cuda.synchronize()
         return bool(torch.equal(ref.view(torch.int32), dst[:lanes].view(torch.int32)))
 
+    def cols_match(p0, nb):
+        """The strip probe's output (dst) against the library's sum_dim(0) of
+        the same [nb/4/p0, p0] view, bit for bit."""
+        rows = (nb // 4) // p0
+        xs = N.Desc(src.data_ptr(), [rows, p0], N.F32, 0)
+        ref = torch.empty(p0, dtype=torch.float32, device="cuda")
+        N.check(lib.rtc_sum_dim(xs.ref, 0, N.Desc(ref.data_ptr(), [p0], N.F32, 0).ref))
+        torch.cuda.synchronize()
+        return bool(torch.equal(ref.view(torch.int32), dst[:p0].view(torch.int32)))
+
     def timeit(name, mode, nb, algo_bytes, p0, p1, p2, dirty=False):
         """dirty=False: L2 flushed by writing 256 MiB and then reading another
         256 MiB, so the timed kernel starts on clean lines; dirty=True: the
@@ -845,6 +855,8 @@ def run_probe(args) -> None:
                 "l2": "dirty" if dirty else "clean", "repeat": args.repeat}
         if mode == 8:
             line["matches_sum_dim"] = lanes_match(p0, nb)
+        if mode == 9:
+            line["matches_sum_dim"] = cols_match(p0, nb)
         print(json.dumps(line), flush=True)
 
     # u < 0: the stats kernel with float32 trees per float4 (|u| loads in flight)
@@ -860,6 +872,13 @@ def run_probe(args) -> None:
     for warps in (-2322, 802, 804, 808, 1202, 1204, 1602, 1604, 1608):
         timeit(f"lane sum [8192,16384] warps/CTA {warps}", 8, 4 * R3 * C3, 4 * R3 * C3 + 4 * R3,
                C3, warps, 0)
+    # cfg4's broadcast_add_backward onto [1, C]: a dim-0 sum of [32768, 4096];
+    # p1 columns per CTA, p2 = 100 * rows per tile + ring stages
+    # (W >= 1000: the run-time-width kernel for W - 1000 columns)
+    for w, code in ((1016, 25606), (16, 25606), (32, 25606), (1032, 25606), (32, 12808),
+                    (16, 12808), (8, 25608), (4, 25608), (64, 12806)):
+        timeit(f"strip dim0 [{R4},{C4}] W{w} p{code}", 9, 4 * R4 * C4, 4 * R4 * C4 + 4 * C4,
+               C4, w, code)
     for dirty in (False, True):
         tag = "dirty-L2" if dirty else "clean-L2"
         timeit(f"{tag} cfg1 add->mul_scalar product", 5, 8 * N1, 12 * N1, 0, 4, 32, dirty)

@@ -124,17 +124,14 @@ rtc_result rtc_selftest_ordered_sum(const rtc_tensor* x, int chains, float init,
  * mish, softplus) and softmax; no reference counterpart.
  *  RTC_MATH_TOLERANCE (default): within 1e-6 relative error or 4 ulp of the
  *    reference's result on every float input, from single-precision
- *    exp/tanh/log (at most 5.8e-7 relative over all 2^32 inputs for the
- *    forward activations, 8.0e-7 for gelu_backward); where the reference's
- *    own formula cancels (gelu's 1 + tanh for inputs below -1.58,
- *    gelu_backward's there and around its zero near -0.75, softplus and
- *    mish's 1 + exp) the result is the reference's bit for bit.
+ *    exp/tanh/log (at most 5.8e-7 relative over all 2^32 inputs); where the
+ *    reference's own formula cancels (gelu's 1 + tanh for inputs below
+ *    -1.58, softplus and mish's 1 + exp) the exact glibc steps are kept.
  *  RTC_MATH_EXACT: glibc's expf/tanhf reproduced bit for bit (softplus and
  *    mish still use a correctly rounded log: within 1 and 6 ulp).
  * Process-wide; the environment variable RTC_MATH_MODE=exact|tolerance sets
  * the initial mode.  Kernels already queued keep the mode they were queued
- * with.  ELU, SELU, the other backward ops and the losses are the same in
- * both. */
+ * with.  ELU, SELU, the backward ops and the losses are the same in both. */
 enum { RTC_MATH_TOLERANCE = 0, RTC_MATH_EXACT = 1 };
 rtc_result rtc_set_math_mode(int mode);
 int rtc_get_math_mode(void);
@@ -422,8 +419,7 @@ rtc_result rtc_sigmoid_backward(const rtc_tensor* grad_output, const rtc_tensor*
  * output. */
 rtc_result rtc_tanh_backward(const rtc_tensor* grad_output, const rtc_tensor* output,
                              const rtc_tensor* grad_input);
-/* GeluBackward (ops.rs:3102-3125), from the saved input: glibc's tanhf bit
- * for bit in RTC_MATH_EXACT, the tolerance rule in RTC_MATH_TOLERANCE. */
+/* GeluBackward (ops.rs:3102-3125), from the saved input, with glibc tanhf. */
 rtc_result rtc_gelu_backward(const rtc_tensor* grad_output, const rtc_tensor* input,
                              const rtc_tensor* grad_input);
 /* autograd's GELU forward (ops.rs:3131-3141), which rounds its cubic term as

@@ -26,14 +26,21 @@ struct GradSigmoid {
 struct GradTanh {
   RT_HD float operator()(float g, float y) const { return fmul(g, fsub(1.0f, fmul(y, y))); }
 };
-// ops.rs:3110-3118: inner = k * (x + 0.044715*((x*x)*x)), t = tanh(inner),
-// then gelu_grad_finish (rt_ops.cuh); glibc's tanhf bit for bit
+// ops.rs:3110-3118, with k = sqrt(2/pi) in f32 and c3 = 3 * 0.044715 in f32:
+//   inner = k * (x + 0.044715*((x*x)*x));  t = tanh(inner);  sech2 = 1 - t*t
+//   d_inner = k * (1 + (c3*x)*x)
+//   grad = g * (0.5*(1 + t) + ((0.5*x)*sech2)*d_inner)
 struct GradGelu {
   float k, c3;
   RT_HD float operator()(float g, float x) const {
     const float x3 = fmul(fmul(x, x), x);
     const float inner = fmul(k, fadd(x, fmul(0.044715f, x3)));
-    return gelu_grad_finish(k, c3, g, x, tanhf_glibc(inner));
+    const float t = tanhf_glibc(inner);
+    const float sech2 = fsub(1.0f, fmul(t, t));
+    const float d_inner = fmul(k, fadd(1.0f, fmul(fmul(c3, x), x)));
+    const float a = fmul(0.5f, fadd(1.0f, t));
+    const float b = fmul(fmul(fmul(0.5f, x), sech2), d_inner);
+    return fmul(g, fadd(a, b));
   }
 };
 // ops.rs:3136-3141 (autograd gelu_forward, not ops::gelu):
@@ -111,9 +118,7 @@ cudaError_t launch_grad_unary(GradUnaryOp op, const float* g, const float* saved
     case kGradTanh: return launch_map(GradTanh{}, in, out, n, s);
     case kGradGelu: {
       volatile float three = 3.0f, c = 0.044715f;
-      const float c3 = three * c;
-      return math_exact() ? launch_map(GradGelu{gelu_k(), c3}, in, out, n, s)
-                          : launch_map_split(GradGeluTol{gelu_k(), c3}, in, out, n, s);
+      return launch_map(GradGelu{gelu_k(), three * c}, in, out, n, s);
     }
   }
   return cudaErrorInvalidValue;

@@ -78,7 +78,7 @@ cudaError_t launch_unary(UnaryOp op, float param, const float* x, float* out, si
       return exact ? launch_map(OpTanh{}, in, out, n, s) : launch_map(OpTanhTol{}, in, out, n, s);
     case kGelu:
       return exact ? launch_map(OpGelu{gelu_k()}, in, out, n, s)
-                   : launch_map_split(OpGeluTol{gelu_k()}, in, out, n, s);
+                   : launch_map_split(OpGeluTol{gelu_k()}, x, out, n, s);
     case kSwish:
       return exact ? launch_map(OpSwish{}, in, out, n, s) : launch_map(OpSwishTol{}, in, out, n, s);
     case kElu: return launch_map(OpElu{param}, in, out, n, s);

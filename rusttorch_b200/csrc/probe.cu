@@ -24,6 +24,11 @@
 //  mode 8  the last-axis sum of src viewed as [bytes/4/p0, p0] (cfg3's
 //          sum_dim(1) for p0 = 16384) into dst by the four-lanes-per-warp
 //          kernel with p1 warps per CTA.
+//  mode 9  the dim-0 sum of src viewed as [bytes/4/p0, p0] (cfg4's
+//          broadcast_add_backward onto [1, C] for p0 = 4096) into dst by the
+//          TMA strip kernel with p1 % 1000 columns per CTA, p2 / 100 rows per
+//          tile and p2 % 100 ring stages (p1 >= 1000: the kernel that takes
+//          the width at run time even for 16 and 32 columns).
 //  mode 7  the global sum/max/min kernel (reduce.cu) in the shape p0
 //          threads, p1 loads in flight per thread, p2 blocks per SM (0: as
 //          many as stay resident), over bytes/4 floats of src; p2 >= 100:
@@ -274,6 +279,14 @@ cudaError_t launch_probe(int mode, const void* src, void* dst, size_t bytes, int
     if (p0 <= 0 || bytes % (4 * (size_t)p0) != 0) return cudaErrorInvalidValue;
     return launch_lane_sum_variant(p1, static_cast<const float*>(src), bytes / 4 / p0, (size_t)p0,
                                    static_cast<float*>(dst), s);
+  }
+  if (mode == 9) {
+    if (p0 <= 0 || p1 <= 0 || p2 <= 0 || bytes % (4 * (size_t)p0) != 0) return cudaErrorInvalidValue;
+    bool used = false;
+    e = launch_strip_tma_shape(kDimSum, static_cast<const float*>(src), 1, bytes / 4 / p0,
+                               (size_t)p0, static_cast<float*>(dst), s, &used, (size_t)(p1 % 1000),
+                               (size_t)(p2 / 100), p2 % 100, p1 < 1000);
+    return e != cudaSuccess ? e : (used ? cudaSuccess : cudaErrorInvalidValue);
   }
   if (mode == 7) {
     StatsPart* parts = nullptr;

@@ -32,4 +32,29 @@ __device__ __forceinline__ void fold_pipelined(const float* p, int s, int n, Ste
   for (; k < n; k++) step(p[k * s]);
 }
 
+// The same with the stride S known at compile time: every load of a batch
+// is an immediate offset from one pointer, which steps once per batch.
+template <int S, class Step>
+__device__ __forceinline__ void fold_pipelined_fixed(const float* p, int n, Step&& step) {
+  int k = 0;
+  if (n >= 8) {
+    float cur[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) cur[u] = p[u * S];
+    const float* q = p + 8 * S;
+    for (k = 8; k + 8 <= n; k += 8, q += 8 * S) {
+      float nxt[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) nxt[u] = q[u * S];
+#pragma unroll
+      for (int u = 0; u < 8; u++) step(cur[u]);
+#pragma unroll
+      for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) step(cur[u]);
+  }
+  for (; k < n; k++) step(p[k * S]);
+}
+
 }  // namespace rt

@@ -137,6 +137,12 @@ cudaError_t launch_reduce_dim(DimReduce op, const float* x, size_t outer, size_t
 // (and launches nothing) when the layout does not suit TMA.
 cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t len,
                              size_t inner, float* out, cudaStream_t s, bool* used);
+// The same with the strip shape given: W columns per CTA (a multiple of 4),
+// R rows per tile, `stages` tiles in the ring; fixed_width: W = 16 and 32
+// use kernels compiled for that width (bench.py's sizing probe compares).
+cudaError_t launch_strip_tma_shape(DimReduce op, const float* x, size_t outer, size_t len,
+                                   size_t inner, float* out, cudaStream_t s, bool* used,
+                                   size_t W, size_t R, int stages, bool fixed_width);
 
 // ------------------------------------------------------- autograd backward
 enum GradUnaryOp { kGradRelu, kGradSigmoid, kGradTanh, kGradGelu };

@@ -485,48 +485,6 @@ RT_HD float tanhf_glibc_ge1(float x) {
   return (f2u(x) >> 31) ? -z : z;
 }
 
-// tanhf for 0.4 <= |x| < 1 only (the band of GELU's gradient that its
-// tolerance rule sends to the exact path, rt_ops.cuh): fdlibm's path for that
-// range, -t/(t + 2) with t = expm1f(-2|x|).  expm1f's argument a = -2|x| lies
-// in (-2, -0.8], beyond ln2/2 in magnitude, so its reduction count is k = -1
-// below 3*ln2/2 and the truncated a/ln2 - 1/2 (-2 or -3) above, and only the
-// reconstructions for k = -1 and k <= -2 remain (selected without branches).
-// Both IEEE divisions go through fdiv_markstein: expm1f's (numerator near -2,
-// denominator in [4.9, 7.1]) and -t/(t + 2) (numerator in [0.55, 0.87),
-// denominator in [1.13, 1.45]).  Bit-identical to glibc's tanhf on every float
-// of that range (tests/native/libm_check).
-RT_HD float tanhf_glibc_mid(float x) {
-  const float kLn2Hi = u2f(0x3f317180u), kLn2Lo = u2f(0x3717f7d1u);
-  const float kInvLn2 = u2f(0x3fb8aa3bu);
-  const float kQ1 = u2f(0xbd088889u), kQ2 = u2f(0x3ad00d01u), kQ3 = u2f(0xb8a670cdu);
-  const float kQ4 = u2f(0x36867e54u), kQ5 = u2f(0xb457edbbu);
-  const uint32_t ha = f2u(x) & 0x7fffffffu;
-  const float a = fmul(-2.0f, u2f(ha));
-  const bool km1 = f2u(a) < 0xbf851592u;        // |a| < 3*ln2/2 (a < 0: bits grow with |a|)
-  const int k = km1 ? -1 : (int)fsub(fmul(kInvLn2, a), 0.5f);   // truncation toward 0
-  const float tk = (float)k;
-  const float hi = fsub(a, fmul(tk, kLn2Hi));
-  const float lo = fmul(tk, kLn2Lo);
-  const float xr = fsub(hi, lo);
-  const float c = fsub(fsub(hi, xr), lo);
-  const float hfx = fmul(0.5f, xr);
-  const float hxs = fmul(xr, hfx);
-  float poly = fadd(kQ4, fmul(hxs, kQ5));
-  poly = fadd(kQ3, fmul(hxs, poly));
-  poly = fadd(kQ2, fmul(hxs, poly));
-  poly = fadd(kQ1, fmul(hxs, poly));
-  const float r1 = fadd(1.0f, fmul(hxs, poly));
-  const float t3 = fsub(3.0f, fmul(r1, hfx));
-  const float e = fmul(hxs, fdiv_markstein(fsub(r1, t3), fsub(6.0f, fmul(xr, t3))));
-  const float e2 = fsub(fsub(fmul(xr, fsub(e, c)), c), hxs);
-  // k = -1: (xr - e2)/2 - 1/2;  k <= -2: (1 - (e2 - xr)) * 2^k - 1
-  const float t_m1 = fsub(fmul(0.5f, fsub(xr, e2)), 0.5f);
-  const float t_le2 = fsub(u2f(f2u(fsub(1.0f, fsub(e2, xr))) + ((uint32_t)k << 23)), 1.0f);
-  const float t = km1 ? t_m1 : t_le2;
-  const float q = fdiv_markstein(-t, fadd(t, 2.0f));
-  return (f2u(x) >> 31) ? -q : q;
-}
-
 // tanhf, bit-identical to glibc's (fdlibm single-precision algorithm),
 // without branches: fdlibm returns +-1 for |x| >= 22 (and for +-inf) from
 // special cases, and its common path already rounds to exactly +-1 for every

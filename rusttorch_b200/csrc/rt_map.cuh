@@ -143,129 +143,99 @@ cudaError_t launch_map(const F& f, const In<NIN>& in, float* out, size_t n, cuda
 
 
 // Map for a rule with a cheap path and an expensive one that only some
-// elements need (GELU and its gradient in the tolerance math mode).  The last
-// of the NIN inputs is x; F provides arg(x) -> z, fast(z, &cls) (the cheap
-// result, and cls = 0 when it is final, 1 or 2 when exact_a(z) or exact_b(z)
-// must replace it) and finish(ins..., x, t).  Every thread runs the cheap path
-// on its elements; the arguments that need an exact path are queued in the
-// warp's shared memory (slot = the warp's running count plus the lanes below
-// in a ballot), class 1 from the front of the queue and class 2 from the
-// back, so that the whole warp then evaluates the queue 32 arguments at a
-// time with one class per pass except where the two meet; each element picks
-// up its result from its slot.  So the expensive paths run on full warps,
-// once per queued element, instead of on every warp that holds one such
-// element (which, for inputs spread as the BASELINE configs are, is every
-// warp).  Results equal F's per-element operator() bit for bit.
-template <int NIN>
-constexpr int split_u() { return NIN == 1 ? 2 : 1; }   // 16-byte vectors per input per lane
+// elements need (GELU in the tolerance math mode): F provides arg(x),
+// needs_exact(z), fast_tanh(z), exact_tanh(z) and finish(x, t).  Every
+// thread runs the cheap path on its elements; the arguments of the elements
+// that need the expensive path are queued in the warp's shared memory (slot
+// = the warp's running count plus the lanes below in a ballot), the whole
+// warp then evaluates the queue 32 arguments at a time, and each element
+// picks up its result from its slot.  So the expensive path runs on full
+// warps, once per queued element, instead of on every warp that holds one
+// such element (which, for inputs spread as the BASELINE configs are, is
+// every warp).  Results equal F's per-element operator() bit for bit.
+constexpr int kSplitU = 2;
 
-template <class F, int NIN>
-__device__ __forceinline__ float split_finish(const F& f, const float (*xs)[4 * split_u<NIN>()], int e,
-                                              float t) {
-  if constexpr (NIN == 1) return f.finish(xs[0][e], t);
-  else return f.finish(xs[0][e], xs[1][e], t);
-}
-
-template <class F, int NIN>
+template <class F>
 __global__ void __launch_bounds__(kThreads)
-map_split_kernel(In<NIN> in, float* out, size_t n, F f) {
-  constexpr int U = split_u<NIN>();
-  constexpr int E = 4 * U;              // elements per lane per iteration
-  constexpr int CAP = 32 * E;           // queue slots per warp
-  __shared__ float queue[kThreads / 32][CAP];
+map_split_kernel(const float* x, float* out, size_t n, F f) {
+  __shared__ float queue[kThreads / 32][32 * 4 * kSplitU];
   const unsigned lane = threadIdx.x & 31u;
   float* wq = queue[threadIdx.x >> 5];
   const unsigned below = (1u << lane) - 1u;
   const size_t n4 = n >> 2;
-  const size_t tile = (size_t)kThreads * U;
+  const size_t tile = (size_t)kThreads * kSplitU;
   const size_t step = (size_t)gridDim.x * tile;
   // Every lane of a warp runs the same number of iterations (the loop bound
   // is the warp's first index), so the ballots see all 32 lanes.
   const size_t warp0 = (size_t)blockIdx.x * tile + (threadIdx.x & ~31u);
-  auto load = [&](size_t wbase, float4 (*v)[U]) {
+  auto load = [&](size_t wbase, float4* v) {
 #pragma unroll
-    for (int u = 0; u < U; u++) {
+    for (int u = 0; u < kSplitU; u++) {
       const size_t j = wbase + lane + (size_t)u * kThreads;
-#pragma unroll
-      for (int k = 0; k < NIN; k++)
-        v[k][u] = j < n4 ? ld4(in.p[k] + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u] = j < n4 ? ld4(x + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
-  float4 cur[NIN][U], nxt[NIN][U];
+  float4 cur[kSplitU], nxt[kSplitU];
   if (warp0 < n4) load(warp0, cur);
   for (size_t wbase = warp0; wbase < n4; wbase += step) {
     const size_t base = wbase + lane;
-    float xs[NIN][E], t[E];
-    int slot[E];
+    float xs[4 * kSplitU], t[4 * kSplitU];
+    int slot[4 * kSplitU];
 #pragma unroll
-    for (int k = 0; k < NIN; k++)
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        xs[k][4 * u] = cur[k][u].x;
-        xs[k][4 * u + 1] = cur[k][u].y;
-        xs[k][4 * u + 2] = cur[k][u].z;
-        xs[k][4 * u + 3] = cur[k][u].w;
-      }
+    for (int u = 0; u < kSplitU; u++) {
+      xs[4 * u] = cur[u].x;
+      xs[4 * u + 1] = cur[u].y;
+      xs[4 * u + 2] = cur[u].z;
+      xs[4 * u + 3] = cur[u].w;
+    }
     // the next iteration's loads are in flight during this one's arithmetic
     if (wbase + step < n4) load(wbase + step, nxt);
-    int na = 0, nb = 0;
+    int count = 0;
 #pragma unroll
-    for (int e = 0; e < E; e++) {
-      const float z = f.arg(xs[NIN - 1][e]);
-      int cls;
-      t[e] = F::fast(z, &cls);
-      if (base + (size_t)(e / 4) * kThreads >= n4) cls = 0;
-      const unsigned ma = __ballot_sync(0xffffffffu, cls == 1);
-      const unsigned mb = __ballot_sync(0xffffffffu, cls == 2);
-      slot[e] = cls == 1 ? na + __popc(ma & below)
-                         : (cls == 2 ? CAP - 1 - nb - __popc(mb & below) : -1);
-      if (cls) wq[slot[e]] = z;
-      na += __popc(ma);
-      nb += __popc(mb);
+    for (int e = 0; e < 4 * kSplitU; e++) {
+      const float z = f.arg(xs[e]);
+      const bool valid = base + (size_t)(e / 4) * kThreads < n4;
+      const bool need = valid && F::needs_exact(z);
+      t[e] = F::fast_tanh(z);
+      const unsigned m = __ballot_sync(0xffffffffu, need);
+      slot[e] = need ? count + __popc(m & below) : -1;
+      if (need) wq[slot[e]] = z;
+      count += __popc(m);
     }
     __syncwarp();
-    for (int j = (int)lane; j < na + nb; j += 32) {
-      if (j < na) {
-        wq[j] = F::exact_a(wq[j]);
-      } else {
-        const int q = CAP - 1 - (j - na);
-        wq[q] = F::exact_b(wq[q]);
-      }
-    }
+    for (int k = (int)lane; k < count; k += 32) wq[k] = F::exact_tanh(wq[k]);
     __syncwarp();
 #pragma unroll
-    for (int e = 0; e < E; e++)
+    for (int e = 0; e < 4 * kSplitU; e++)
       if (slot[e] >= 0) t[e] = wq[slot[e]];
     __syncwarp();
 #pragma unroll
-    for (int u = 0; u < U; u++) {
+    for (int u = 0; u < kSplitU; u++) {
       const size_t j = base + (size_t)u * kThreads;
       if (j < n4)
-        st4(out + 4 * j, make_float4(split_finish<F, NIN>(f, xs, 4 * u, t[4 * u]),
-                                     split_finish<F, NIN>(f, xs, 4 * u + 1, t[4 * u + 1]),
-                                     split_finish<F, NIN>(f, xs, 4 * u + 2, t[4 * u + 2]),
-                                     split_finish<F, NIN>(f, xs, 4 * u + 3, t[4 * u + 3])));
-#pragma unroll
-      for (int k = 0; k < NIN; k++) cur[k][u] = nxt[k][u];
+        st4(out + 4 * j, make_float4(F::finish(xs[4 * u], t[4 * u]),
+                                     F::finish(xs[4 * u + 1], t[4 * u + 1]),
+                                     F::finish(xs[4 * u + 2], t[4 * u + 2]),
+                                     F::finish(xs[4 * u + 3], t[4 * u + 3])));
+      cur[u] = nxt[u];
     }
   }
   if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
     const size_t i = (n4 << 2) + threadIdx.x;
-    out[i] = apply1<F, NIN>(f, in, i);
+    out[i] = f(x[i]);
   }
 }
 
-template <class F, int NIN>
-cudaError_t launch_map_split(const F& f, const In<NIN>& in, float* out, size_t n, cudaStream_t s) {
+template <class F>
+cudaError_t launch_map_split(const F& f, const float* x, float* out, size_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  bool vec = aligned16(out);
-  for (int k = 0; k < NIN; k++) vec = vec && aligned16(in.p[k]);
-  if (vec) {
+  if (aligned16(x) && aligned16(out)) {
     const unsigned grid =
-        grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * split_u<NIN>(), 32);
-    map_split_kernel<F, NIN><<<grid, kThreads, 0, s>>>(in, out, n, f);
+        grid_for(std::max<size_t>(n >> 2, 1), (size_t)kThreads * kSplitU, 32);
+    map_split_kernel<F><<<grid, kThreads, 0, s>>>(x, out, n, f);
   } else {
-    map_scalar_kernel<F, NIN><<<grid_for(n, kThreads), kThreads, 0, s>>>(in, out, n, f);
+    In<1> in{{x}};
+    map_scalar_kernel<F, 1><<<grid_for(n, kThreads), kThreads, 0, s>>>(in, out, n, f);
   }
   return cudaGetLastError();
 }

@@ -168,50 +168,14 @@ struct OpMishTol {
   }
 };
 
-// GELU's tanh in the tolerance math mode.  1 + tanh(z) cancels for z well
-// below 0: there the reference's result is the gap between -1 and glibc's
-// tanhf(z), and it carries no more than a few of tanhf's bits, so those must
-// be glibc's to the last bit.  For 1 <= |z| < 22 glibc's tanhf is
-// 1 - q, q = 2*RN(1/RN(expm1f(2|z|) + 2)), rounded once more (tanhf_glibc_ge1);
-// 1 - q lies in [0.5, 1), where floats are 2^-24 apart, so the reference's
-// 1 + tanhf(z) = 1 - RN(1 - q) is q rounded to a multiple of 2^-24.  The fast
-// path has r = 1/(e^(2|z|) + 1) in hand (tanh_fast_abs's t = 1 - 2r), so
-// g = 2r * 2^24 estimates q * 2^24.  Over every float z with 1 <= |z| <= 9.1,
-// |2r - q| <= 0.707 * 2^-22 * 2r (measured on the host, all 2^31 such
-// floats): when g lies closer than 0.5 - 2^-22 * g to an integer n, q * 2^24
-// rounds to n as well, without a tie, and the reference's 1 + tanhf(z) is
-// exactly n * 2^-24; tanh is then returned as n * 2^-24 - 1 (exact), which
-// gives the reference's bits in every later step.  Otherwise (about 16 q of
-// the arguments: all of them above z = -2.2, a few per cent below -3) the
-// argument goes to the exact path.  Above exact_below the fast tanh's error,
-// magnified by the cancellation, stays within the tolerance; below -9.1
-// glibc's tanhf is exactly -1, as is t (2r < 2^-25 there).
-// cls: 0 = the returned tanh is final, 1 = the exact path is needed.
-RT_HD float gelu_tanh_fast(float z, float exact_below, int* cls) {
-  const float az = fabs_bits(z);
-  int k;
-  const float p = exp_core(fmul(2.0f, az > 9.5f ? 9.5f : az), &k);
-  // 1/(e^(2|z|) + 1); 2|z| <= 19 keeps 2^k one normal power of two
-  const float r = rcp_cr(fadd(fmul(p, u2f((uint32_t)(k + 127) << 23)), 1.0f));
-  const float t = u2f(f2u(ffma(-2.0f, r, 1.0f)) | (f2u(z) & 0x80000000u));
-  *cls = 0;
-  if (z < exact_below && z >= -9.1f) {
-    const float g = fmul(r, 33554432.0f);                        // 2r * 2^24, exact
-    const float n = fsub(fadd(g, 12582912.0f), 12582912.0f);      // nearest integer (g < 2^22)
-    if (fabs_bits(fsub(g, n)) < fsub(0.5f, fmul(g, u2f(0x34800000u))))   // 0.5 - g * 2^-22
-      return fsub(fmul(n, u2f(0x33800000u)), 1.0f);              // n * 2^-24 - 1
-    *cls = 1;
-  }
-  return t;
-}
-
-// :61 gelu = 0.5x * (1 + tanh(z)), z = sqrt(2/pi) * (x + 0.044715 x^3).  The
-// fast tanh's error stays within the tolerance above z = kGeluExactBelow
-// (1 + tanh(z) > 0.115 there: the cancellation magnifies it by less than 9,
-// and the result stays within 5.8e-7 of the reference's); below, the result
-// is the reference's bit for bit, from the shortcut of gelu_tanh_fast or from
-// tanhf_glibc_ge1.  map_split_kernel (rt_map.cuh) runs the exact path on
-// full warps.
+// :61 gelu.  1 + tanh(z) cancels for z well below 0: there the reference's
+// result is the gap between -1 and glibc's tanhf(z), and it carries no more
+// than a few of tanhf's bits, so tanhf must be glibc's to the last bit
+// (tanhf_glibc).  Above kGeluExactBelow (1 + tanh(z) > 0.115) the
+// cancellation magnifies the fast tanh's error by less than 9 and the result
+// stays within 5.8e-7 of the reference's; below -9.1 glibc's tanhf is
+// exactly -1.  The kernel sends only the middle range through
+// tanhf_glibc (rt_map.cuh, map_split_kernel).
 #ifndef RT_GELU_EXACT_BELOW
 #define RT_GELU_EXACT_BELOW -1.4f
 #endif
@@ -223,59 +187,14 @@ struct OpGeluTol {
     const float x3 = fmul(fmul(x, x), x);
     return fmul(k, fadd(x, fmul(0.044715f, x3)));
   }
-  RT_HD static float fast(float z, int* cls) { return gelu_tanh_fast(z, kGeluExactBelow, cls); }
-  RT_HD static float exact_a(float z) { return tanhf_glibc_ge1(z); }   // 1.4 < |z| <= 9.1
-  RT_HD static float exact_b(float z) { return tanhf_glibc_ge1(z); }   // (not produced)
+  RT_HD static bool needs_exact(float z) { return z < kGeluExactBelow && z >= -9.1f; }
+  // -1 exactly below -8.9 (2/(e^(2|z|) + 1) < 2^-25 there), as glibc's tanhf
+  RT_HD static float fast_tanh(float z) { return tanh_fast_abs(z); }
+  RT_HD static float exact_tanh(float z) { return tanhf_glibc_ge1(z); }   // 1.4 < |z| <= 9.1
   RT_HD static float finish(float x, float t) { return fmul(fmul(0.5f, x), fadd(1.0f, t)); }
   RT_HD float operator()(float x) const {
     const float z = arg(x);
-    int cls;
-    const float t = fast(z, &cls);
-    return finish(x, cls ? exact_a(z) : t);
-  }
-};
-
-// autograd/ops.rs:3110-3118, GELU's gradient given t = tanh(inner), with
-// k = sqrt(2/pi) and c3 = 3 * 0.044715 in f32:
-//   sech2 = 1 - t*t;  d_inner = k * (1 + (c3*x)*x)
-//   grad = g * (0.5*(1 + t) + ((0.5*x)*sech2)*d_inner)
-RT_HD float gelu_grad_finish(float k, float c3, float g, float x, float t) {
-  const float sech2 = fsub(1.0f, fmul(t, t));
-  const float d_inner = fmul(k, fadd(1.0f, fmul(fmul(c3, x), x)));
-  const float a = fmul(0.5f, fadd(1.0f, t));
-  const float b = fmul(fmul(fmul(0.5f, x), sech2), d_inner);
-  return fmul(g, fadd(a, b));
-}
-
-// GELU's gradient in the tolerance math mode, from gelu_tanh_fast's tanh
-// except in two ranges of inner = z (checked on the host over every float x,
-// tests/test_fastmath.py): z in [-0.95, -0.45), around the zero of the
-// gradient (x near -0.75), where a + b cancels and only glibc's tanhf bits
-// give the reference's result (tanhf_glibc_mid, class 2); and z below
-// kGeluGradExactBelow, where 1 + t and 1 - t*t cancel (gelu_tanh_fast's
-// certified shortcut, else tanhf_glibc_ge1, class 1).  Between -1.45 and
-// -0.95, above -0.45 and for every z > 0 the fast tanh keeps the gradient
-// within 1e-6 relative error or 4 ulp of the reference's.
-constexpr float kGeluGradExactBelow = -1.45f;
-struct GradGeluTol {
-  float k, c3;
-  RT_HD float arg(float x) const {
-    const float x3 = fmul(fmul(x, x), x);
-    return fmul(k, fadd(x, fmul(0.044715f, x3)));
-  }
-  RT_HD static float fast(float z, int* cls) {
-    const float t = gelu_tanh_fast(z, kGeluGradExactBelow, cls);
-    if (z >= -0.95f && z < -0.45f) *cls = 2;
-    return t;
-  }
-  RT_HD static float exact_a(float z) { return tanhf_glibc_ge1(z); }   // 1.45 < |z| <= 9.1
-  RT_HD static float exact_b(float z) { return tanhf_glibc_mid(z); }   // 0.45 < |z| <= 0.95
-  RT_HD float finish(float g, float x, float t) const { return gelu_grad_finish(k, c3, g, x, t); }
-  RT_HD float operator()(float g, float x) const {
-    const float z = arg(x);
-    int cls;
-    const float t = fast(z, &cls);
-    return finish(g, x, cls == 1 ? exact_a(z) : (cls == 2 ? exact_b(z) : t));
+    return finish(x, needs_exact(z) ? exact_tanh(z) : fast_tanh(z));
   }
 };
 

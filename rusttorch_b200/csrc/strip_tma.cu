@@ -25,10 +25,14 @@ namespace {
 constexpr int kMaxStages = 8;
 constexpr int kStageAlign = 128;            // bytes; TMA destinations are 16-byte aligned
 
-template <int OP>
+// WT > 0: the strip width W known at compile time, so a column's chain walks
+// the tile with immediate offsets (one pointer step per eight rows) instead
+// of a multiply-add per element; WT = 0: W at run time.
+template <int OP, int WT>
 __global__ void __launch_bounds__(288)
 strip_tma_kernel(const __grid_constant__ CUtensorMap tm, const float* x, size_t len,
-                 size_t inner, int W, int R, int S, size_t strips, float* out, int* err) {
+                 size_t inner, int W_rt, int R, int S, size_t strips, float* out, int* err) {
+  const int W = WT > 0 ? WT : W_rt;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
@@ -97,15 +101,20 @@ strip_tma_kernel(const __grid_constant__ CUtensorMap tm, const float* x, size_t 
       return;
     }
     const int rows = (int)min((size_t)R, len - st * R);
-    if (tid < w_eff)
-      fold_pipelined(ring + slot * stage_floats + tid, W, rows, [&](float v) {
-        if (OP == kDimMax) {
-          nan |= v != v;
-          acc = fmaxf(acc, v);
-        } else {
-          acc = fadd(acc, v);
-        }
-      });
+    auto step = [&](float v) {
+      if (OP == kDimMax) {
+        nan |= v != v;
+        acc = fmaxf(acc, v);
+      } else {
+        acc = fadd(acc, v);
+      }
+    };
+    if (tid < w_eff) {
+      if constexpr (WT > 0)
+        fold_pipelined_fixed<WT>(ring + slot * stage_floats + tid, rows, step);
+      else
+        fold_pipelined(ring + slot * stage_floats + tid, W, rows, step);
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (++slot == S) {
@@ -142,10 +151,7 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
   if ((reinterpret_cast<uintptr_t>(x) & 15u) || inner % 4 || inner < 4 || len == 0 ||
       len >= (1ull << 31) || inner >= (1ull << 31) || outer >= (1ull << 31))
     return cudaSuccess;
-  const int dev = cur_device();
-  int* err = wait_timeout_flag(dev);
-  if (!err) return cudaSuccess;
-  const int sms = sm_count(dev);
+  const int sms = sm_count(cur_device());
   // Every CTA folds its strip over all `len` rows, so a second, partial wave
   // of CTAs would nearly double the time: pick the narrowest strip (at
   // least 32 columns, when there are enough columns) whose CTAs all fit on
@@ -168,9 +174,7 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
   W = std::min<size_t>(32, std::max<size_t>(4, (W + 3) & ~size_t(3)));
   while (W < 256 && outer * ((inner + W - 1) / W) > resident(W)) W += 16;
   W = std::min(W, inner);
-  const size_t strips = (inner + W - 1) / W;
-  const size_t ctas = outer * strips;
-  if (ctas >= (1ull << 31)) return cudaSuccess;
+  const size_t ctas = outer * ((inner + W - 1) / W);
   size_t R = rows_for(W);
   size_t stage = smem_for(W) / S;
   // With at most two CTAs per SM (few, narrow strips: e.g. 4096 columns
@@ -183,6 +187,30 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
     stage = ((R * W * sizeof(float) + kStageAlign - 1) / kStageAlign) * kStageAlign;
     stages = (int)std::min<size_t>(kMaxStages, std::max<size_t>(2, half / stage));
   }
+  return launch_strip_tma_shape(op, x, outer, len, inner, out, st, used, W, R, stages, true);
+}
+
+// The launch for a given strip width W (columns per CTA), tile height R and
+// ring depth; *used = false (nothing launched) when the shape cannot be
+// encoded or does not fit in shared memory.  W is a multiple of 4, so every
+// strip's first column c0 = s*W — the tiles' innermost TMA coordinate —
+// starts on a 16-byte boundary.
+cudaError_t launch_strip_tma_shape(DimReduce op, const float* x, size_t outer, size_t len,
+                                   size_t inner, float* out, cudaStream_t st, bool* used,
+                                   size_t W, size_t R, int stages, bool fixed_width) {
+  *used = false;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) || inner % 4 || inner < 4 || len == 0 ||
+      len >= (1ull << 31) || inner >= (1ull << 31) || outer >= (1ull << 31) || W < 4 ||
+      W % 4 || W > 256 || W > inner || R < 1 || R > 256 || R > len || stages < 2 ||
+      stages > kMaxStages)
+    return cudaSuccess;
+  const int dev = cur_device();
+  int* err = wait_timeout_flag(dev);
+  if (!err) return cudaSuccess;
+  const size_t strips = (inner + W - 1) / W;
+  const size_t ctas = outer * strips;
+  if (ctas >= (1ull << 31)) return cudaSuccess;
+  const size_t stage = ((R * W * sizeof(float) + kStageAlign - 1) / kStageAlign) * kStageAlign;
   const size_t smem = stage * stages;
   if (smem > (227u << 10)) return cudaSuccess;
 
@@ -193,23 +221,30 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
   if (!encode_tensor_map_f32(&tm, x, 3, dims, strides, box)) return cudaSuccess;
 
   const int threads = ((int)((W + 31) / 32) + 1) * 32;
-  cudaError_t e = cudaSuccess;
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    kernel<<<(unsigned)ctas, threads, smem, st>>>(tm, x, len, inner, (int)W, (int)R, stages,
+                                                  strips, out, err);
+    return cudaGetLastError();
+  };
+  cudaError_t e = cudaErrorInvalidValue;
+  const int wt = fixed_width ? (int)W : 0;
   switch (op) {
-#define RT_STRIP_TMA(OPV)                                                                    \
-  case OPV:                                                                                  \
-    e = cudaFuncSetAttribute(strip_tma_kernel<OPV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)smem);                                                     \
-    if (e != cudaSuccess) return e;                                                          \
-    strip_tma_kernel<OPV><<<(unsigned)ctas, threads, smem, st>>>(tm, x, len, inner, (int)W,  \
-                                                                 (int)R, stages, strips, out, err); \
+#define RT_STRIP_TMA(OPV)                                               \
+  case OPV:                                                             \
+    e = wt == 16   ? go(strip_tma_kernel<OPV, 16>)                      \
+        : wt == 32 ? go(strip_tma_kernel<OPV, 32>)                      \
+                   : go(strip_tma_kernel<OPV, 0>);                      \
     break;
     RT_STRIP_TMA(kDimSum)
     RT_STRIP_TMA(kDimMean)
     RT_STRIP_TMA(kDimMax)
 #undef RT_STRIP_TMA
   }
-  *used = true;
-  return cudaGetLastError();
+  if (e == cudaSuccess) *used = true;
+  return e;
 }
 
 }  // namespace rt

@@ -36,12 +36,6 @@ float ref(int which, float x) {
     }
     case 6: return expf(x);                                            // exp
     case 7: return x >= 1.17549435e-38f && x <= 3.40282347e38f ? logf(x) : NAN;  // log
-    case 8: {                                 // gelu_backward, grad_output 1 (autograd/ops.rs)
-      const float k = gelu_k(), c3 = 3.0f * 0.044715f;
-      const float t = tanhf(k * (x + 0.044715f * ((x * x) * x)));
-      const float d_inner = k * (1.0f + (c3 * x) * x);
-      return 1.0f * (0.5f * (1.0f + t) + ((0.5f * x) * (1.0f - t * t)) * d_inner);
-    }
     default: return NAN;
   }
 }
@@ -61,7 +55,6 @@ float mine(int which, float x) {
       // log_fast's domain: positive normal floats
       return (u >= 0x00800000u && u < 0x7f800000u) ? rt::log_fast(x) : NAN;
     }
-    case 8: return rt::GradGeluTol{gelu_k(), 3.0f * 0.044715f}(1.0f, x);
     default: return NAN;
   }
 }
@@ -77,12 +70,6 @@ int64_t ordered(float f) {
 // The device rule evaluated on the host, for comparison with GPU results.
 extern "C" void fm_eval(int which, const float* x, float* out, uint64_t n) {
   for (uint64_t i = 0; i < n; i++) out[i] = mine(which, x[i]);
-}
-// GELU's gradient as the device computes it in the tolerance mode, with
-// grad_output g.
-extern "C" void fm_eval_gelu_grad(const float* g, const float* x, float* out, uint64_t n) {
-  const rt::GradGeluTol rule{gelu_k(), 3.0f * 0.044715f};
-  for (uint64_t i = 0; i < n; i++) out[i] = rule(g[i], x[i]);
 }
 extern "C" void fm_ref(int which, const float* x, float* out, uint64_t n) {
   for (uint64_t i = 0; i < n; i++) out[i] = ref(which, x[i]);
@@ -152,56 +139,6 @@ extern "C" uint64_t fm_scan(int which, uint64_t start, uint64_t stop, uint64_t s
     worst[1] = w;
   }
   return c;
-}
-
-// GELU (which 5) or its gradient (8) over inputs u = start, start+stride, ...
-// < stop: counts the inputs whose z = sqrt(2/pi)*(x + 0.044715x^3) takes the
-// certified shortcut of gelu_tanh_fast (z in [-9.1, cut), 1 + tanh(z) taken
-// as a multiple of 2^-24) and, of those, the ones whose result differs in
-// any bit from the reference's; counts[2] = inputs sent to an exact path.
-extern "C" void fm_gelu_shortcut(int which, uint64_t start, uint64_t stop, uint64_t stride,
-                                 int threads, uint64_t* counts) {
-  if (threads < 1) threads = 1;
-  std::vector<uint64_t> c0(threads, 0), c1(threads, 0), c2(threads, 0);
-  std::vector<std::thread> pool;
-  const uint64_t count = stop > start ? (stop - start + stride - 1) / stride : 0;
-  const float k = gelu_k();
-  for (int t = 0; t < threads; t++) {
-    pool.emplace_back([&, t] {
-      for (uint64_t i = count * t / threads; i < count * (t + 1) / threads; i++) {
-        const uint32_t u = (uint32_t)(start + i * stride);
-        float x;
-        memcpy(&x, &u, 4);
-        if (isnan(x)) continue;
-        const float z = rt::OpGeluTol{k}.arg(x);
-        int cls;
-        if (which == 5) rt::OpGeluTol::fast(z, &cls);
-        else rt::GradGeluTol::fast(z, &cls);
-        if (cls) {
-          c2[t]++;
-          continue;
-        }
-        const float cut = which == 5 ? rt::kGeluExactBelow : rt::kGeluGradExactBelow;
-        if (!(z < cut && z >= -9.1f)) continue;
-        c0[t]++;
-        const float a = ref(which, x), b = mine(which, x);
-        uint32_t ua, ub;
-        memcpy(&ua, &a, 4);
-        memcpy(&ub, &b, 4);
-        if (ua != ub) c1[t]++;
-      }
-    });
-  }
-  uint64_t a = 0, b = 0, c = 0;
-  for (int t = 0; t < threads; t++) {
-    pool[t].join();
-    a += c0[t];
-    b += c1[t];
-    c += c2[t];
-  }
-  counts[0] = a;
-  counts[1] = b;
-  counts[2] = c;
 }
 
 // Softmax along the last axis of a [rows, len] array as the device computes

@@ -213,14 +213,7 @@ def test_gpu_grad_unary(name, n):
     elif name == "tanh":
         saved = O.unary("tanh", x)
     want = O.grad_unary(name, g, saved)
-    fn = getattr(rt, name + "_backward")
-    if name == "gelu":
-        # glibc's tanhf bit for bit in the exact math mode; the tolerance
-        # mode's rule is checked in tests/test_tolerance_gpu.py
-        with rt.math_mode("exact"):
-            got = fn(rt.Tensor.from_numpy(g), rt.Tensor.from_numpy(saved))
-    else:
-        got = fn(rt.Tensor.from_numpy(g), rt.Tensor.from_numpy(saved))
+    got = getattr(rt, name + "_backward")(rt.Tensor.from_numpy(g), rt.Tensor.from_numpy(saved))
     assert_bits_equal(got.to_numpy(), want, name)
 
 

@@ -98,51 +98,6 @@ def test_cfg4_full_size(fm, op):
         assert_bits_equal(got, host_rule(fm, op, x.ravel()).reshape(x.shape), "gelu cfg4 host")
 
 
-def host_gelu_grad(fm, g, x):
-    out = np.empty_like(x)
-    fm.fm_eval_gelu_grad(g.ctypes.data, x.ctypes.data, out.ctypes.data, x.size)
-    return out
-
-
-def test_gelu_backward_bit_sweep(fm):
-    """GELU's gradient over every 257th float bit pattern, grad_output
-    normal(0, 2): equal to the host build, within tolerance of the oracle."""
-    x = bit_sweep(257)
-    g = O.normal(x.size, 71, 0.0, 2.0)
-    got = rt.gelu_backward(dev(g), dev(x)).to_numpy()
-    assert_bits_equal(got, host_gelu_grad(fm, g, x), "gelu_backward vs its host build")
-    assert_within_tolerance(got, O.grad_unary("gelu", g, x), "gelu_backward vs oracle")
-
-
-def test_gelu_backward_cfg4_full_size(fm):
-    x = O.normal(32768 * 4096, 4, 0.0, 2.0)
-    g = O.normal(x.size, 10, 0.0, 1.0)
-    got = rt.gelu_backward(dev(g), dev(x)).to_numpy()
-    assert_within_tolerance(got, O.grad_unary("gelu", g, x), "gelu_backward cfg4")
-    assert_bits_equal(got, host_gelu_grad(fm, g, x), "gelu_backward cfg4 host")
-
-
-@pytest.mark.parametrize("lo,hi", [(-6.0, -1.0), (-1.2, -0.5), (-1.5, 3.0), (0.0, 8.0),
-                                   (-12.0, -8.0)])
-@pytest.mark.parametrize("n", [1, 7, 4096 + 3, 1 << 20])
-def test_gelu_backward_split_queue(fm, lo, hi, n):
-    """The two-input split kernel with both exact classes (the band around
-    the gradient's zero and the negative tail) queued, one of them, or none;
-    ragged tails; and the scalar path for misaligned data."""
-    x = O.uniform(n + 1, 62, lo, hi)
-    g = O.normal(n + 1, 63, 0.0, 1.0)
-    got = rt.gelu_backward(dev(g[:n]), dev(x[:n])).to_numpy()
-    assert_bits_equal(got, host_gelu_grad(fm, g[:n], x[:n]), f"gelu_backward [{lo},{hi}) n={n}")
-    tg, tx = dev(g), dev(x)
-    out = rt.Tensor.from_numpy(np.zeros(n + 1, np.float32))
-    vg = rt.Tensor.from_device_ptr(tg.ptr + 4, [n], owner=tg)
-    vx = rt.Tensor.from_device_ptr(tx.ptr + 4, [n], owner=tx)
-    vo = rt.Tensor.from_device_ptr(out.ptr + 4, [n], owner=out)
-    N.check(N.lib().rtc_gelu_backward(vg.desc, vx.desc, vo.desc))
-    assert_bits_equal(vo.to_numpy(), host_gelu_grad(fm, g[1:], x[1:]),
-                      f"misaligned gelu_backward n={n}")
-
-
 @pytest.mark.parametrize("lo,hi", [(-6.0, -1.0), (-1.5, 3.0), (0.0, 8.0), (-12.0, -8.0)])
 @pytest.mark.parametrize("n", [1, 7, 4096 + 3, 1 << 20])
 def test_gelu_split_queue(fm, lo, hi, n):
