@@ -181,13 +181,18 @@ cudaError_t launch_strip_tma(DimReduce op, const float* x, size_t outer, size_t 
   // folded over many rows) each CTA can take tiles of 256 rows and a deeper
   // ring at no cost in residency, keeping two CTAs' rings within an SM.
   int stages = S;
-  if (ctas <= 2 * (size_t)sms) {
+  // The compiled-in widths pay off where the chains are long and few CTAs
+  // share an SM ([1, C] gradient of cfg4: 0.48 -> 0.62); with many CTAs per
+  // SM (cfg3's dim-0 sums) the run-time-width kernel measured 0.966 against
+  // 0.943.
+  const bool few = ctas <= 2 * (size_t)sms;
+  if (few) {
     const size_t half = (size_t)(227u << 10) / 2 - 1024;   // one of two CTAs per SM
     R = std::min<size_t>({len, 256, std::max<size_t>(8, half / 2 / (W * sizeof(float)))});
     stage = ((R * W * sizeof(float) + kStageAlign - 1) / kStageAlign) * kStageAlign;
     stages = (int)std::min<size_t>(kMaxStages, std::max<size_t>(2, half / stage));
   }
-  return launch_strip_tma_shape(op, x, outer, len, inner, out, st, used, W, R, stages, true);
+  return launch_strip_tma_shape(op, x, outer, len, inner, out, st, used, W, R, stages, few);
 }
 
 // The launch for a given strip width W (columns per CTA), tile height R and
