@@ -416,7 +416,13 @@ def main() -> None:
     # all-reduce runs on a second stream, overlapped with the ops after it;
     # the next step's sum (which overwrites the partial) and the end of the
     # timed region wait for it.  Its own duration is recorded on that stream.
-    comm = torch.cuda.Stream() if world > 1 else None
+    # The stream has the highest priority: the block scheduler then places the
+    # collective's CTAs as soon as the sum's CTAs leave, ahead of the softmax
+    # and AdamW CTAs queued behind them on the step's stream; at normal
+    # priority AdamW's grid can hold every SM until it ends, and the
+    # all-reduce (which waits for all ranks) then finishes only after the
+    # slowest rank's AdamW, stalling the next step's sum.
+    comm = torch.cuda.Stream(priority=-1) if world > 1 else None
 
     def run_op(op, coll_ev=None):
         if op == "add_mul_scalar":
