@@ -10,9 +10,8 @@ BASELINE.json config:
 Strong scaling (default): on N GPUs rank r owns elements [r*n/N, (r+1)*n/N)
 of cfg1, cfg2 and cfg5 and rows [r*32768/N, (r+1)*32768/N) of cfg4, cut from
 the same seeded streams as the N = 1 tensors.  The sum's per-GPU f64
-partials are combined by an NCCL all-reduce, the only exchange (on a second
-stream, overlapped with the ops after it; the step waits for it); the other
-ops need none.  `--scaling weak` gives every GPU a full-size copy instead.
+partials are all-reduced over peer memory (NVLink) by the library, the only
+exchange (at the end of the step, after AdamW); the other ops need none.  `--scaling weak` gives every GPU a full-size copy instead.
 value = algorithmic bytes of the whole step / max-over-ranks device time.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
@@ -392,59 +391,63 @@ def main() -> None:
 
     # Before timing (N > 1): the sharded sum/max/min of cfg2 through the
     # exact per-shard summaries, all-gathered and folded in rank order,
-    # against the NCCL all-reduce of the f64 partials the timed step uses.
+    # against the peer-memory all-reduce of the f64 partials the timed step
+    # uses (and against NCCL's all-reduce of the same partials).
     check = None
+    peer = None
     sum_dev = torch.zeros(1, dtype=torch.float64, device="cuda")
+    sum_all = torch.zeros(1, dtype=torch.float64, device="cuda")
     if world > 1 and "sum" in ops:
         from rusttorch_b200 import sharded as sh
         exact = sh.ShardedReducer(lib, rank, world).stats(D["x2"])
+        peer = sh.PeerSum(lib, rank, world, local)
         N.check(lib.rtc_sum_device(D["x2"].ref, c_void_p(sum_dev.data_ptr())))
-        dist.all_reduce(sum_dev)
-        got = float(sum_dev.item())
+        peer.allreduce(sum_dev.data_ptr(), sum_all.data_ptr())
+        N.check(lib.rtc_synchronize())
+        got = float(sum_all.item())
+        nccl = sum_dev.clone()
+        dist.all_reduce(nccl)
         absx = torch.tensor([float(bufs["x2"].abs().double().sum())], dtype=torch.float64,
                             device="cuda")
         dist.all_reduce(absx)
         tol = 1e-6 * float(absx.item())
         if abs(got - exact[0]) > tol:
-            raise SystemExit(f"sharded sum mismatch: all-reduce {got!r} vs rank-order {exact[0]!r}")
+            raise SystemExit(f"sharded sum mismatch: peer all-reduce {got!r} vs rank-order "
+                             f"{exact[0]!r}")
         check = {"sum": exact[0], "mean": exact[1], "max": exact[2], "min": exact[3],
-                 "allreduce_sum_minus_exact": got - exact[0], "tolerance": tol}
+                 "allreduce_sum_minus_exact": got - exact[0],
+                 "nccl_allreduce_sum_minus_exact": float(nccl.item()) - exact[0],
+                 "tolerance": tol}
 
     # The sum lands in device memory without a host round trip; at N > 1 the
-    # per-GPU f64 partials are combined by an NCCL all-reduce (the hot path's
-    # only exchange).  Nothing in the step reads the combined sum, so the
-    # all-reduce runs on a second stream, overlapped with the ops after it;
-    # the next step's sum (which overwrites the partial) and the end of the
-    # timed region wait for it.  Its own duration is recorded on that stream.
-    # The stream has the highest priority: the block scheduler then places the
-    # collective's CTAs as soon as the sum's CTAs leave, ahead of the softmax
-    # and AdamW CTAs queued behind them on the step's stream; at normal
-    # priority AdamW's grid can hold every SM until it ends, and the
-    # all-reduce (which waits for all ranks) then finishes only after the
-    # slowest rank's AdamW, stalling the next step's sum.
-    comm = torch.cuda.Stream(priority=-1) if world > 1 else None
-
-    def run_op(op, coll_ev=None):
+    # per-GPU f64 partials are combined (the hot path's only exchange) at the
+    # end of the step, after AdamW, where every rank arrives after the same
+    # work, by the library's peer-memory all-reduce (sharded.PeerSum: one
+    # kernel per rank writes its partial into every rank's slots over NVLink
+    # and adds the slots in rank order).  NCCL's all-reduce of the 8 bytes
+    # cost 0.2-0.7 ms a step here, varying from run to run, at the end of the
+    # step or on a second stream right after the sum (there it also waited
+    # for the slowest rank's AdamW, whose grid holds every SM).
+    def run_op(op):
         if op == "add_mul_scalar":
             N.check(lib.rtc_add_mul_scalar(D["a"].ref, D["b"].ref, 0.5, D["c"].ref))
         elif op == "sum":
-            if comm is not None:
-                stream.wait_stream(comm)           # the last all-reduce has read sum_dev
             N.check(lib.rtc_sum_device(D["x2"].ref, c_void_p(sum_dev.data_ptr())))
-            if comm is not None:
-                comm.wait_stream(stream)
-                with torch.cuda.stream(comm):
-                    if coll_ev is not None:
-                        coll_ev[0].record(comm)
-                    dist.all_reduce(sum_dev)
-                    if coll_ev is not None:
-                        coll_ev[1].record(comm)
         elif op == "softmax":
             N.check(lib.rtc_softmax(D["x4"].ref, 1, D["y4"].ref))
         elif op == "adamw":
             lr, b1, b2, eps, wd, t = ADAMW
             N.check(lib.rtc_adamw_update(D["p"].ref, D["g"].ref, D["m"].ref, D["v"].ref, lr, b1,
                                          b2, eps, wd, t, D["p"].ref, D["m"].ref, D["v"].ref))
+
+    def combine(coll_ev=None):
+        """The step's exchange: the sum's per-GPU partials all-reduced."""
+        if peer is not None:
+            if coll_ev is not None:
+                coll_ev[0].record(stream)
+            peer.allreduce(sum_dev.data_ptr(), sum_all.data_ptr())
+            if coll_ev is not None:
+                coll_ev[1].record(stream)
 
     def barrier():
         if world > 1:
@@ -453,8 +456,7 @@ def main() -> None:
     for _ in range(args.warmup):
         for op in ops:
             run_op(op)
-    if comm is not None:
-        stream.wait_stream(comm)
+        combine()
     torch.cuda.synchronize()
 
     # Events around every op of every step; the ops' inputs are re-read only
@@ -469,15 +471,23 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        if world > 1:
+            # The GPU idles 20 ms (untimed) while this process queues all K
+            # steps, so no step waits for the host (the clock sampler's
+            # thread can hold Python's lock for milliseconds); then one
+            # untimed exchange lines the ranks up, since they leave the
+            # barrier above at different host times and every step's
+            # exchange would otherwise absorb that skew.
+            torch.cuda._sleep(40_000_000)
+            combine()
         start.record(stream)
         for k in range(args.steps):
             for op in ops:
                 e0, e1 = ev[op][k]
                 e0.record(stream)
-                run_op(op, coll[k])
+                run_op(op)
                 e1.record(stream)
-        if comm is not None:
-            stream.wait_stream(comm)               # the step includes the last all-reduce
+            combine(coll[k])
         stop.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -502,7 +512,7 @@ def main() -> None:
                   "frac_of_8TBs_spec": L.bytes[o] / (op_ms[o] * 1e-3) / 1e9 / SPEC_HBM_GBS}
               for o in ops}
     if world > 1 and "sum" in ops:
-        per_op["sum"]["nccl_allreduce_ms"] = coll_ms
+        per_op["sum"]["peer_allreduce_ms"] = coll_ms
     dom = max(ops, key=lambda o: op_ms[o])
     achieved = L.bytes[dom] / (op_ms[dom] * 1e-3) / 1e9
     traffic = None
@@ -513,8 +523,8 @@ def main() -> None:
             if len(parts) >= 3 and parts[0] == dom:
                 # bytes per element, from the ncu capture, times this launch's elements
                 traffic = int(round(float(parts[2]) * L.elems[dom]))
-    gpu_launches = args.steps * sum({"add_mul_scalar": 1, "sum": 2, "softmax": 1,
-                                     "adamw": 1}[o] for o in ops)
+    gpu_launches = args.steps * (sum({"add_mul_scalar": 1, "sum": 2, "softmax": 1,
+                                      "adamw": 1}[o] for o in ops) + (peer is not None))
 
     # e2e: the same step through the C ABI from pinned host buffers.
     e2e = None
@@ -561,6 +571,8 @@ def main() -> None:
         if check is not None:
             line["sharded_check"] = check
         print(json.dumps(line), flush=True)
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -340,6 +340,30 @@ rtc_result rtc_sharded_adamw_update(const rtc_tensor* params, const rtc_tensor* 
                                     double epsilon, double weight_decay, uint64_t timestep,
                                     size_t n_shards);
 
+/* One process per GPU: the global sum's exchange over peer memory (no
+ * reference counterpart; the reference has no multi-device path).  Each rank
+ * allocates a slot array of rtc_peer_slot_bytes(world) bytes with rtc_malloc
+ * (a whole allocation: IPC maps allocations, not offsets into them), zeroes
+ * it, passes its handle (rtc_ipc_handle) to the other ranks by any host
+ * channel, and opens theirs (rtc_ipc_open).  Then
+ * rtc_peer_allreduce_sum_f64(device, local, slots, world, rank, g, out), with
+ * slots[p] = rank p's slot array as mapped on this rank (its own for p =
+ * rank) and g = 1, 2, 3, ... on successive calls (the same g on every rank),
+ * writes into *out (device) the sum of every rank's *local, added in rank
+ * order from 0.0 — the same bits on every rank.  Queued on the calling
+ * thread's stream, one kernel; it waits at most 2 s for the other ranks, then
+ * writes NaN and raises the flag rtc_synchronize reports.  rtc_ipc_close
+ * unmaps a peer's array (before the peer frees it). */
+#define RTC_IPC_HANDLE_BYTES 64
+#define RTC_PEER_MAX_RANKS 8
+rtc_result rtc_ipc_handle(int device, const void* dev_ptr, void* handle_out);
+rtc_result rtc_ipc_open(int device, const void* handle, void** dev_ptr_out);
+rtc_result rtc_ipc_close(int device, void* dev_ptr);
+size_t rtc_peer_slot_bytes(int world);
+rtc_result rtc_peer_allreduce_sum_f64(int device, const double* local, void* const* slots,
+                                      int world, int rank, unsigned long long generation,
+                                      double* out);
+
 /* -------------------------------------------------------- broadcasting */
 /* ops::add_broadcast / sub_broadcast / mul_broadcast / div_broadcast
  * (ops/broadcast.rs:177-198): NumPy broadcasting of a and b (dtype checked

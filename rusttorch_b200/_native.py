@@ -17,6 +17,8 @@ HEADER_PATH = PKG.parent / "include" / "rusttorch_cuda.h"
 
 # math modes (rtc_set_math_mode)
 MATH_TOLERANCE, MATH_EXACT = 0, 1
+# peer-memory exchange (rtc_peer_allreduce_sum_f64)
+IPC_HANDLE_BYTES, PEER_MAX_RANKS = 64, 8
 # dtype codes and status codes (rusttorch_cuda.h)
 F32, F64, I32, I64 = 0, 1, 2, 3
 OK, SHAPE_MISMATCH, DTYPE_MISMATCH, EMPTY_TENSOR, INVALID_DIMENSION, INVALID_ARGUMENT, \
@@ -132,6 +134,12 @@ _SIGNATURES = {
     "rtc_sharded_max_dim": (RtcResult, [T, c_size_t, T, c_size_t]),
     "rtc_sharded_adamw_update": (RtcResult, [T, T, T, T, c_double, c_double, c_double, c_double,
                                              c_double, c_uint64, c_size_t]),
+    "rtc_ipc_handle": (RtcResult, [c_int, c_void_p, c_void_p]),
+    "rtc_ipc_open": (RtcResult, [c_int, c_void_p, POINTER(c_void_p)]),
+    "rtc_ipc_close": (RtcResult, [c_int, c_void_p]),
+    "rtc_peer_slot_bytes": (c_size_t, [c_int]),
+    "rtc_peer_allreduce_sum_f64": (RtcResult, [c_int, c_void_p, POINTER(c_void_p), c_int, c_int,
+                                               c_uint64, c_void_p]),
     "rtc_selftest_bounded_wait": (RtcResult, []),
     "rtc_selftest_ordered_sum": (RtcResult, [T, c_int, c_float, POINTER(c_float)]),
     "rtc_add_broadcast": (RtcResult, [T, T, T]),

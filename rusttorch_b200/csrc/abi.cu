@@ -59,8 +59,8 @@ extern "C" rtc_result rtc_synchronize(void) {
   cudaGetDevice(&device);
   if (take_wait_timeouts(device))
     return fail(RTC_BACKEND_ERROR,
-                "a kernel gave up waiting for a shared-memory tile (2 s limit); "
-                "results since the last synchronize are incomplete");
+                "a kernel gave up waiting (for a shared-memory tile or another rank; "
+                "2 s limit); results since the last synchronize are incomplete");
   return ok();
 }
 

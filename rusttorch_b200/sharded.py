@@ -99,3 +99,69 @@ class ShardedReducer:
 
     def close(self) -> None:
         pass
+
+
+class PeerSum:
+    """The sum of one f64 per rank (each rank's partial of a sharded sum),
+    over peer memory: every rank's library writes its partial into a slot on
+    every rank's GPU through a CUDA IPC mapping and adds the slots in rank
+    order (rtc_peer_allreduce_sum_f64) — one kernel, no NCCL call, no host
+    round trip.  Construct on every rank of the default process group (one
+    process per GPU, all on one node); the IPC handles travel once, through
+    torch.distributed.  Call close() on every rank before the process group
+    is destroyed."""
+
+    def __init__(self, lib, rank: int, world: int, device: int):
+        import torch.distributed as dist
+
+        if world > N.PEER_MAX_RANKS:
+            raise ValueError(f"at most {N.PEER_MAX_RANKS} ranks")
+        self.lib, self.rank, self.world, self.device = lib, rank, world, device
+        self.generation = 0
+        nbytes = lib.rtc_peer_slot_bytes(world)
+        own = ctypes.c_void_p()
+        N.check(lib.rtc_malloc(device, nbytes, ctypes.byref(own)))
+        self._own = own
+        zero = (ctypes.c_char * nbytes)()
+        N.check(lib.rtc_memcpy_h2d(device, own, zero, nbytes))
+        handle = (ctypes.c_char * N.IPC_HANDLE_BYTES)()
+        N.check(lib.rtc_ipc_handle(device, own, handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        self._opened = []
+        ptrs = (ctypes.c_void_p * world)()
+        for p in range(world):
+            if p == rank:
+                ptrs[p] = own.value
+                continue
+            h = (ctypes.c_char * N.IPC_HANDLE_BYTES).from_buffer_copy(handles[p])
+            mapped = ctypes.c_void_p()
+            N.check(lib.rtc_ipc_open(device, h, ctypes.byref(mapped)))
+            self._opened.append(mapped)
+            ptrs[p] = mapped.value
+        self._ptrs = ptrs
+        dist.barrier()   # every rank's slots are zeroed and mapped
+
+    def allreduce(self, local_ptr: int, out_ptr: int) -> None:
+        """Queues *out = sum over ranks of *local (device f64 pointers) on the
+        library's stream of the calling thread."""
+        self.generation += 1
+        N.check(self.lib.rtc_peer_allreduce_sum_f64(
+            self.device, ctypes.c_void_p(local_ptr), self._ptrs, self.world, self.rank,
+            self.generation, ctypes.c_void_p(out_ptr)))
+
+    def close(self) -> None:
+        """Unmaps the other ranks' slots and frees this rank's (after a
+        barrier, so no rank still writes into them)."""
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        N.check(self.lib.rtc_synchronize())
+        dist.barrier()
+        for m in self._opened:
+            N.check(self.lib.rtc_ipc_close(self.device, m))
+        self._opened = []
+        dist.barrier()
+        N.check(self.lib.rtc_free(self.device, self._own))
+        self._own = None

@@ -246,3 +246,20 @@ def test_nvtx_ranges_switched_on_by_the_environment():
     N.lib().rtc_free_error_message(r.error_msg)
     assert not r.success
     assert out.stdout.strip() == want
+
+
+def test_peer_allreduce_argument_errors():
+    """rtc_peer_allreduce_sum_f64 checks its arguments before touching a
+    device: world beyond RTC_PEER_MAX_RANKS, a rank outside the world, a
+    missing slot array, generation 0."""
+    lib = N.lib()
+    assert lib.rtc_peer_slot_bytes(8) == 2 * 8 * 16
+    assert lib.rtc_peer_slot_bytes(0) == 0
+    fake = ctypes.c_void_p(256)
+    ptrs = (ctypes.c_void_p * 2)(256, 512)
+    nulls = (ctypes.c_void_p * 2)(None, None)
+    for world, rank, slots, gen in ((N.PEER_MAX_RANKS + 1, 0, ptrs, 1), (2, 2, ptrs, 1),
+                                    (2, 0, nulls, 1), (2, 0, ptrs, 0)):
+        with pytest.raises(N.RusttorchError) as e:
+            N.check(lib.rtc_peer_allreduce_sum_f64(0, fake, slots, world, rank, gen, fake))
+        assert e.value.code == N.INVALID_ARGUMENT
