@@ -481,7 +481,7 @@ rtc_result rtc_broadcast_add_backward(const rtc_tensor* grad_output, const rtc_t
 
 /* ------------------------------------------------------------ diagnostics */
 /* Bandwidth probes (no reference counterpart): the read ceiling the
- * reductions are judged against and the sizing of the small fused map.
+ * reductions are measured against and the sizing of the small fused map.
  * mode 0/1: read `bytes` of src with 16-byte loads, p1 (4, 8, 16) loads in
  * flight per thread, p0 threads per block, p2 blocks per SM (0: grid-stride,
  * 1: one contiguous range per block); 2/3: read src through a cp.async.bulk

@@ -1,6 +1,6 @@
 // probe.cu — bandwidth probes (diagnostics; no counterpart in the reference).
 //
-// They measure what the streaming kernels of this library are judged
+// They measure what the streaming kernels of this library are measured
 // against: how fast one B200 can READ HBM (the global and per-lane
 // reductions only read), in two forms, beside a plain copy and the sizing
 // variants of the small fused add->mul_scalar map.
