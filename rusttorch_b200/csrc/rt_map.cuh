@@ -112,11 +112,12 @@ template <class F, class = void>
 struct is_light : std::false_type {};
 template <class F>
 struct is_light<F, std::void_t<decltype(F::kLight)>> : std::bool_constant<F::kLight> {};
-// Functors with `static constexpr bool kHeavy = true` (the exact tanh, GELU,
-// softplus and mish: 90-200 instructions per element) take one vector per
-// thread per iteration: their registers then hold one element group's
-// intermediates, and the SM's many warps supply the parallelism (mish 5 %,
-// softplus 2 % faster; the lighter exp-based ops are faster with four).
+// Functors with `static constexpr bool kHeavy = true` (the exact tanh, GELU
+// and its gradient, softplus and mish: 90-200 instructions per element) take
+// one vector per thread per iteration: their registers then hold one element
+// group's intermediates, and the SM's many warps supply the parallelism
+// (mish 5 %, softplus 2 %, GELU's gradient 9 % faster; the lighter exp-based
+// ops are faster with four).
 template <class F, class = void>
 struct is_heavy : std::false_type {};
 template <class F>
