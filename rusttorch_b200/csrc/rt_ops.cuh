@@ -149,6 +149,7 @@ struct OpTanhTol {
 // reference's float bit for bit (expf_glibc): for x well below 0 its last bit
 // decides the result's leading digits, and only the log is approximated.
 struct OpSoftplusTol {
+  static constexpr bool kHeavy = true;   // one vector per thread per iteration
   RT_HD float operator()(float x) const {
     // !(x <= 20): x > 20, or x NaN (returned as is); below, 1 + exp(x) is a
     // positive normal float in [1, 4.9e8]
